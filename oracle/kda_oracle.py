@@ -1,0 +1,248 @@
+"""CPU oracle for SimpleTrain's KDA chunked scan -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product: only ``tests/``,
+``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference``
+legs of ``bench.py`` may import it.  The CUDA product path never calls it.
+
+What it restates
+----------------
+SimpleTrain's effective KDA implementation is the pure-PyTorch chunk loop
+``_kda_chunked_scan_torch`` (``kernels/kda_kernel.py:244-297``); its Triton
+kernel never launches (the wrapper passes an autotuned meta-parameter
+explicitly, ``kernels/kda_kernel.py:75-92,232``, and the error is swallowed
+into that same torch path at ``:235-238``).  Per chunk of length L
+(``:269-275``), with the running fp32 state S (zero-initialised at ``:264``):
+
+    scores  = tril(Q_c K_c^T)                              (:279-280)
+    o       = scores V_c + Q_c S                           (:281-287)
+    y_c     = (o * g_c).to(y.dtype)   (gate optional)      (:288-290)
+    S       = decay**L * S + U_c                           (:293-295)
+
+The reference computes ``U_c = einsum("bhpd,bhqd->bhpq", K_c, V_c)``, i.e.
+``K_c V_c^T`` -- an [L, L] time-by-time matrix that only broadcasts into the
+[D, D] state when L == D (``:294``).  Two modes are restated here:
+
+* ``literal``   -- exactly that (valid when D == chunk and every chunk that is
+                   followed by another one is full); pinned bit-for-bit in
+                   spirit against the reference itself by
+                   ``tests/golden/make_golden.py``.
+* ``corrected`` -- ``U_c = K_c^T V_c`` ([D, D]), the state update the
+                   docstrings (``:9``, ``models/kimi_k3.py:67``) and README
+                   describe; every shape works.
+
+``decay`` is a Python float (the reference's type, ``:308``) or a tensor that
+broadcasts against the ``[B, H, D, D]`` state as ``[B, H, D, 1]`` (per key
+channel), which the reference's ``decay ** L * state`` also accepts.
+
+The extensions over the reference (an initial state, the returned final state)
+are plain additions to the same loop.  ``manual_backward`` restates, in
+float64, the two-direction backward that the CUDA kernels implement, including
+the closed-form decay gradient, so the algorithm itself is checked against
+autograd on the CPU.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple, Union
+
+import torch
+
+Decay = Union[float, torch.Tensor]
+
+
+# --------------------------------------------------------------------------- #
+# helpers
+# --------------------------------------------------------------------------- #
+def max_rel(x: torch.Tensor, ref: torch.Tensor) -> float:
+    """Normwise max-relative error: max|x - ref| / max|ref| (0 if ref == 0 and x == ref)."""
+    x = x.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    num = (x - ref).abs().max().item() if x.numel() else 0.0
+    den = ref.abs().max().item() if ref.numel() else 0.0
+    if den == 0.0:
+        return 0.0 if num == 0.0 else float("inf")
+    return num / den
+
+
+def decay_bhd1(decay: Decay, B: int, H: int, D: int, dtype=torch.float32) -> Decay:
+    """Map the extended API's decay shapes onto the reference's broadcast form.
+
+    Accepts a float, or a tensor of shape (), (H,), (H, D), (B, H, D) or any
+    shape broadcastable to (B, H, D).  Returns a float or a [B, H, D, 1] tensor
+    (``kernels/kda_kernel.py:295`` broadcasts it against [B, H, D, D]).
+    """
+    if not torch.is_tensor(decay):
+        return float(decay)
+    d = decay.to(dtype)
+    if d.dim() == 1 and d.shape[0] == H and H != D:
+        d = d.view(H, 1)
+    elif d.dim() == 1 and d.shape[0] == H and H == D:
+        d = d.view(H, 1)          # (H,) always means per head in the extended API
+    return d.expand(B, H, D).unsqueeze(-1)
+
+
+# --------------------------------------------------------------------------- #
+# forward restatement
+# --------------------------------------------------------------------------- #
+def chunk_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               gate: Optional[torch.Tensor], decay: Decay, chunk_size: int,
+               initial_state: Optional[torch.Tensor] = None,
+               mode: str = "corrected",
+               compute_dtype: torch.dtype = torch.float32) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Chunked gated linear attention, returning (y, final_state).
+
+    Follows ``kernels/kda_kernel.py:258-297``: inputs are up-cast to the
+    compute dtype (``:259-261``), y is allocated like q (``:263``) and each
+    chunk's output is cast back to q's dtype (``:290``).  ``mode`` picks the
+    state update (see the module docstring).  Differentiable by autograd.
+    """
+    if mode not in ("corrected", "literal"):
+        raise ValueError(f"mode must be 'corrected' or 'literal', got {mode!r}")
+    B, H, T, D = q.shape
+    qf, kf, vf = q.to(compute_dtype), k.to(compute_dtype), v.to(compute_dtype)
+    gf = gate.to(compute_dtype) if gate is not None else None
+    if torch.is_tensor(decay):
+        decay = decay.to(compute_dtype)
+
+    y = torch.empty_like(q)
+    pieces = []
+    if initial_state is None:
+        state = torch.zeros(B, H, D, D, dtype=compute_dtype)
+    else:
+        state = initial_state.to(compute_dtype)
+    causal = torch.ones(chunk_size, chunk_size, dtype=compute_dtype).tril()
+
+    for t0 in range(0, T, chunk_size):
+        t1 = min(T, t0 + chunk_size)
+        L = t1 - t0
+        Qc, Kc, Vc = qf[:, :, t0:t1], kf[:, :, t0:t1], vf[:, :, t0:t1]
+        scores = torch.matmul(Qc, Kc.transpose(-1, -2)) * causal[:L, :L]
+        out = torch.matmul(scores, Vc) + torch.matmul(Qc, state)
+        if gf is not None:
+            out = out * gf[:, :, t0:t1]
+        pieces.append(out.to(y.dtype))
+        if mode == "literal":
+            update = torch.matmul(Kc, Vc.transpose(-1, -2))      # [L, L]: needs L == D
+        else:
+            update = torch.matmul(Kc.transpose(-1, -2), Vc)      # [D, D]
+        state = (decay ** L) * state + update
+    y = torch.cat(pieces, dim=2) if pieces else y
+    return y, state
+
+
+def reference_literal_y(q, k, v, gate, decay, chunk_size):
+    """Exactly the reference's output convention: y only, literal update."""
+    return chunk_scan(q, k, v, gate, decay, chunk_size, mode="literal")[0]
+
+
+def naive_recurrence(q, k, v, gate, decay: float, chunk_size: int,
+                     initial_state: Optional[torch.Tensor] = None):
+    """Per-token restatement of the corrected chunk form (float64, small cases).
+
+    Token t in chunk c sees S_{c-1} (state before its chunk) plus the causal
+    sum of k_s v_s^T over s <= t inside the chunk; S_c = a^L S_{c-1} + sum k v.
+    Used as an independent known-answer check of ``chunk_scan``.
+    """
+    B, H, T, D = q.shape
+    qd, kd, vd = q.double(), k.double(), v.double()
+    gd = gate.double() if gate is not None else None
+    S = torch.zeros(B, H, D, D, dtype=torch.float64) if initial_state is None else initial_state.double().clone()
+    y = torch.zeros(B, H, T, D, dtype=torch.float64)
+    for t0 in range(0, T, chunk_size):
+        t1 = min(T, t0 + chunk_size)
+        run = torch.zeros_like(S)
+        for t in range(t0, t1):
+            run = run + kd[:, :, t, :, None] * vd[:, :, t, None, :]
+            o = torch.einsum("bhd,bhde->bhe", qd[:, :, t], S + run)
+            y[:, :, t] = o * gd[:, :, t] if gd is not None else o
+        S = (decay ** (t1 - t0)) * S + run
+    return y, S
+
+
+# --------------------------------------------------------------------------- #
+# backward restatement (the algorithm the CUDA kernels implement)
+# --------------------------------------------------------------------------- #
+def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
+                    initial_state: Optional[torch.Tensor], dy: torch.Tensor,
+                    dstate_T: Optional[torch.Tensor] = None, mode: str = "corrected"):
+    """Explicit chunk backward in float64.
+
+    Gradients of  L = <dy, y> + <dstate_T, S_T>  for y, S_T = chunk_scan(...).
+    Forward-direction pass ("A") recomputes S_{c-1} chunk by chunk and gives
+    dq and dg; reverse pass ("B") carries dS and gives dk, dv and d(initial
+    state).  The decay gradient uses a closed form that needs no stored
+    states: with a[i] the per-channel decay and exponents counted in tokens,
+
+        dL/dlog a[i] = sum_t start(c_t) q_t[i] dq_inter_t[i]
+                     - sum_c end(c) <dS_c[i,:], U_c[i,:]>
+                     + T <dS_T[i,:], S_T[i,:]>
+
+    where dq_inter = dO S_{c-1}^T, U_c is the chunk's state update and dS_c
+    the gradient reaching S_c.  (Every state entry is a sum of sources
+    decayed by a^(start(sink) - end(source)); differentiating the exponent
+    splits into a sink part and a source part.)  Returns
+    (dq, dk, dv, dg, d_decay[B,H,D], d_initial_state).
+    """
+    B, H, T, D = q.shape
+    C = chunk_size
+    f = torch.float64
+    Q, K, V = q.to(f), k.to(f), v.to(f)
+    G = gate.to(f) if gate is not None else None
+    DY = dy.to(f)
+    a = decay_bhd.to(f).reshape(B, H, D)
+    S0 = initial_state.to(f) if initial_state is not None else torch.zeros(B, H, D, D, dtype=f)
+    causal = torch.ones(C, C, dtype=f).tril()
+    chunks = [(t0, min(T, t0 + C)) for t0 in range(0, T, C)]
+
+    def update(Kc, Vc):
+        return Kc @ Vc.transpose(-1, -2) if mode == "literal" else Kc.transpose(-1, -2) @ Vc
+
+    dq = torch.zeros_like(Q); dk = torch.zeros_like(K); dv = torch.zeros_like(V)
+    dg = torch.zeros_like(Q) if G is not None else None
+    sink = torch.zeros(B, H, D, dtype=f)
+    source = torch.zeros(B, H, D, dtype=f)
+
+    # pass A: forward direction
+    S = S0.clone()
+    for (t0, t1) in chunks:
+        L = t1 - t0
+        Qc, Kc, Vc, DYc = Q[:, :, t0:t1], K[:, :, t0:t1], V[:, :, t0:t1], DY[:, :, t0:t1]
+        P = (Qc @ Kc.transpose(-1, -2)) * causal[:L, :L]
+        O = P @ Vc + Qc @ S
+        if G is not None:
+            dg[:, :, t0:t1] = DYc * O
+            dO = DYc * G[:, :, t0:t1]
+        else:
+            dO = DYc
+        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        dq_inter = dO @ S.transpose(-1, -2)
+        dq[:, :, t0:t1] = dP @ Kc + dq_inter
+        sink += t0 * (Qc * dq_inter).sum(dim=2)
+        S = (a ** L).unsqueeze(-1) * S + update(Kc, Vc)
+    S_T = S
+
+    # pass B: reverse direction
+    dS = dstate_T.to(f).clone() if dstate_T is not None else torch.zeros(B, H, D, D, dtype=f)
+    for (t0, t1) in reversed(chunks):
+        L = t1 - t0
+        Qc, Kc, Vc, DYc = Q[:, :, t0:t1], K[:, :, t0:t1], V[:, :, t0:t1], DY[:, :, t0:t1]
+        dO = DYc * G[:, :, t0:t1] if G is not None else DYc
+        P = (Qc @ Kc.transpose(-1, -2)) * causal[:L, :L]
+        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        if mode == "literal":
+            dk_inter = dS @ Vc                     # d/dK of K V^T against dS
+            dv_inter = dS.transpose(-1, -2) @ Kc
+            source += t1 * (Kc * dk_inter).sum(dim=-1)     # row i of K V^T is token i
+        else:
+            dk_inter = Vc @ dS.transpose(-1, -2)
+            dv_inter = Kc @ dS
+            source += t1 * (Kc * dk_inter).sum(dim=2)
+        dk[:, :, t0:t1] = dP.transpose(-1, -2) @ Qc + dk_inter
+        dv[:, :, t0:t1] = P.transpose(-1, -2) @ dO + dv_inter
+        dS = Qc.transpose(-1, -2) @ dO + (a ** L).unsqueeze(-1) * dS
+    dS0 = dS
+
+    dlog = sink - source
+    if dstate_T is not None:
+        dlog = dlog + T * (dstate_T.to(f) * S_T).sum(dim=-1)
+    d_decay = torch.where(a != 0, dlog / torch.where(a != 0, a, torch.ones_like(a)), torch.zeros_like(a))
+    return dq, dk, dv, dg, d_decay, dS0
