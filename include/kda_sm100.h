@@ -1,0 +1,141 @@
+/*
+ * kda_sm100.h -- C ABI of the B200 (sm_100a) Kimi Delta Attention chunked scan.
+ *
+ * This is the boundary SimpleTrain's KDA dispatch binds to.  The reference's
+ * operator is the Python function
+ *
+ *     kda_chunked_scan(q, k, v, gate=None, decay=0.99, chunk_size=64,
+ *                      use_triton=True) -> y                (kernels/kda_kernel.py:303-311)
+ *
+ * whose GPU work is the Triton launch in kda_chunked_scan_triton
+ * (kernels/kda_kernel.py:195-238) and, in practice, the torch chunk loop
+ * _kda_chunked_scan_torch (kernels/kda_kernel.py:244-297) plus autograd
+ * through it for the backward pass.  The entry points below replace those:
+ *
+ *   kda_fwd_sm100  <- kda_chunked_scan_triton / _kda_chunked_scan_torch forward
+ *   kda_bwd_sm100  <- autograd through _kda_chunked_scan_torch (:269-296)
+ *
+ * Conventions
+ *   - All tensors are device pointers owned by the caller; nothing is
+ *     allocated, freed or synchronised inside these calls.  Work is enqueued
+ *     on `stream` (a cudaStream_t; NULL = legacy default stream).
+ *   - q, k, v, g, y, dy, dq, dk, dv, dg are [B, H, T, D] views described by
+ *     element strides (the KDA layer passes [B, T, H, D] memory viewed as
+ *     [B, H, T, D], models/kimi_k3.py:99-102).  The innermost stride must be
+ *     1, every other stride a multiple of 8 elements and every base pointer
+ *     16-byte aligned (tensor-memory-accelerator copies need 16-byte rows).
+ *   - States are fp32 [B, H, D, D] contiguous, row index = key channel.
+ *   - decay is either a device fp32 array addressed as
+ *     decay[b*decay_stride_b + h*decay_stride_h + d*decay_stride_d]
+ *     (strides may be 0 to broadcast), or, when `decay` is NULL, the host
+ *     scalar `decay_scalar` (the reference's float decay, :308).  The state
+ *     is scaled per chunk of length L by decay**L along its key-channel rows
+ *     (:295 with decay broadcast as [B, H, D, 1]).
+ *   - Return value: KDA_OK or a kda_status code; nothing throws across the
+ *     ABI.  Errors detected on the device (a bounded wait that expired) are
+ *     OR-ed into *status when `status` is non-NULL and are never fatal to
+ *     the CUDA context.
+ *   - Thread-safe; reentrant per stream.  Two calls that overlap on the GPU
+ *     must not share a workspace.
+ */
+#ifndef KDA_SM100_H
+#define KDA_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_ABI_VERSION 1
+
+typedef struct CUstream_st *kda_stream_t; /* identical to cudaStream_t */
+
+enum kda_dtype { KDA_DTYPE_BF16 = 0, KDA_DTYPE_F16 = 1 };
+
+enum kda_flags {
+  /* Reference-exact state update U_c = K_c V_c^T (kernels/kda_kernel.py:294).
+     Needs D == chunk; a ragged last chunk may not ask for the final state. */
+  KDA_FLAG_LITERAL = 1u << 0,
+};
+
+enum kda_status {
+  KDA_OK = 0,
+  KDA_ERR_NULL_ARGUMENT = 1,   /* a required pointer is NULL */
+  KDA_ERR_BAD_SHAPE = 2,       /* negative size, or literal mode with D != chunk */
+  KDA_ERR_UNSUPPORTED = 3,     /* head dim / chunk / dtype this build has no kernel for */
+  KDA_ERR_BAD_LAYOUT = 4,      /* stride or alignment rule violated */
+  KDA_ERR_WORKSPACE = 5,       /* workspace missing or too small */
+  KDA_ERR_CUDA = 6,            /* a CUDA runtime call or launch failed */
+  KDA_ERR_DEVICE_TIMEOUT = 64, /* device-side: a bounded wait expired (status word bit) */
+};
+
+typedef struct kda_tensor {
+  void *data; /* NULL only where documented optional */
+  int64_t stride_b, stride_h, stride_t, stride_d; /* element strides of the [B,H,T,D] view */
+} kda_tensor;
+
+typedef struct kda_fwd_params {
+  int32_t B, H, T, D; /* batch, heads, tokens, head dim (key dim == value dim) */
+  int32_t chunk;      /* chunk length; 64 */
+  int32_t dtype;      /* enum kda_dtype, for q, k, v, g, y */
+  uint32_t flags;     /* enum kda_flags */
+  kda_tensor q, k, v;
+  kda_tensor g;       /* output gate; g.data == NULL means no gate (:288-289) */
+  kda_tensor y;       /* output */
+  const float *decay; /* NULL -> decay_scalar */
+  int64_t decay_stride_b, decay_stride_h, decay_stride_d;
+  double decay_scalar;
+  const float *state_in; /* [B,H,D,D] initial state; NULL -> zeros (:264) */
+  float *state_out;      /* [B,H,D,D] final state; NULL -> not written */
+  void *workspace;       /* kda_fwd_workspace_bytes() bytes, 256-byte aligned */
+  size_t workspace_bytes;
+  int32_t *status; /* optional device word for device-side errors */
+} kda_fwd_params;
+
+typedef struct kda_bwd_params {
+  int32_t B, H, T, D, chunk, dtype;
+  uint32_t flags;
+  kda_tensor q, k, v, g, dy;     /* forward inputs and dL/dy; g.data may be NULL */
+  kda_tensor dq, dk, dv, dg;     /* outputs; dg ignored when g.data == NULL */
+  const float *decay;
+  int64_t decay_stride_b, decay_stride_h, decay_stride_d;
+  double decay_scalar;
+  const float *state_in;   /* forward's initial state, NULL -> zeros */
+  const float *state_out;  /* forward's final state; required when dstate_out and ddecay are both set */
+  const float *dstate_out; /* dL/d(final state), NULL -> zero */
+  float *dstate_in;        /* out: dL/d(initial state), NULL -> not written */
+  float *ddecay;           /* out: [B,H,D] fp32 dL/d(decay[b,h,d]), NULL -> not computed */
+  void *workspace;
+  size_t workspace_bytes;
+  int32_t *status;
+} kda_bwd_params;
+
+/* Workspace needed by one call (0 allowed).  flags as in the params. */
+size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk,
+                               uint32_t flags);
+size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk,
+                               uint32_t flags);
+
+/* Forward scan: y (and optionally the final state). */
+int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream);
+
+/* Backward scan: dq, dk, dv, dg, and optionally dL/d(initial state), dL/d(decay). */
+int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream);
+
+/* Human-readable text of a kda_status value (static storage). */
+const char *kda_status_string(int32_t status);
+
+/* KDA_ABI_VERSION of the loaded library. */
+int32_t kda_abi_version(void);
+
+/* Number of kernels this library has launched in the process so far
+   (diagnostic; no counterpart in the reference). */
+uint64_t kda_launch_count(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* KDA_SM100_H */

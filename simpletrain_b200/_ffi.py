@@ -1,0 +1,107 @@
+"""ctypes binding of ``include/kda_sm100.h`` (the library's C ABI).
+
+The structures below mirror the header field for field; ``ABI_VERSION`` must
+match ``KDA_ABI_VERSION``.  Loading fails loudly when the library has not been
+built -- there is no other implementation to fall back to.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+
+ABI_VERSION = 1
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libkda_sm100.so")
+
+KDA_DTYPE_BF16 = 0
+KDA_DTYPE_F16 = 1
+KDA_FLAG_LITERAL = 1 << 0
+
+KDA_OK = 0
+KDA_ERR_NULL_ARGUMENT = 1
+KDA_ERR_BAD_SHAPE = 2
+KDA_ERR_UNSUPPORTED = 3
+KDA_ERR_BAD_LAYOUT = 4
+KDA_ERR_WORKSPACE = 5
+KDA_ERR_CUDA = 6
+KDA_ERR_DEVICE_TIMEOUT = 64
+
+EXPORTED = (
+    "kda_fwd_sm100", "kda_bwd_sm100", "kda_fwd_workspace_bytes", "kda_bwd_workspace_bytes",
+    "kda_status_string", "kda_abi_version", "kda_launch_count",
+)
+
+
+class KdaTensor(ctypes.Structure):
+    _fields_ = [("data", c_void_p), ("stride_b", c_int64), ("stride_h", c_int64),
+                ("stride_t", c_int64), ("stride_d", c_int64)]
+
+
+class KdaFwdParams(ctypes.Structure):
+    _fields_ = [
+        ("B", c_int32), ("H", c_int32), ("T", c_int32), ("D", c_int32),
+        ("chunk", c_int32), ("dtype", c_int32), ("flags", c_uint32),
+        ("q", KdaTensor), ("k", KdaTensor), ("v", KdaTensor), ("g", KdaTensor), ("y", KdaTensor),
+        ("decay", c_void_p), ("decay_stride_b", c_int64), ("decay_stride_h", c_int64),
+        ("decay_stride_d", c_int64), ("decay_scalar", c_double),
+        ("state_in", c_void_p), ("state_out", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("status", c_void_p),
+    ]
+
+
+class KdaBwdParams(ctypes.Structure):
+    _fields_ = [
+        ("B", c_int32), ("H", c_int32), ("T", c_int32), ("D", c_int32),
+        ("chunk", c_int32), ("dtype", c_int32), ("flags", c_uint32),
+        ("q", KdaTensor), ("k", KdaTensor), ("v", KdaTensor), ("g", KdaTensor), ("dy", KdaTensor),
+        ("dq", KdaTensor), ("dk", KdaTensor), ("dv", KdaTensor), ("dg", KdaTensor),
+        ("decay", c_void_p), ("decay_stride_b", c_int64), ("decay_stride_h", c_int64),
+        ("decay_stride_d", c_int64), ("decay_scalar", c_double),
+        ("state_in", c_void_p), ("state_out", c_void_p), ("dstate_out", c_void_p),
+        ("dstate_in", c_void_p), ("ddecay", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("status", c_void_p),
+    ]
+
+
+_LIB = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the KDA library (once) and declare its signatures."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise ImportError(
+            f"KDA sm_100a library not found at {path}; build it with "
+            "`python -m simpletrain_b200.build` (needs nvcc)")
+    lib = ctypes.CDLL(path)
+    lib.kda_fwd_sm100.argtypes = [POINTER(KdaFwdParams), c_void_p]
+    lib.kda_fwd_sm100.restype = c_int32
+    lib.kda_bwd_sm100.argtypes = [POINTER(KdaBwdParams), c_void_p]
+    lib.kda_bwd_sm100.restype = c_int32
+    for fn in (lib.kda_fwd_workspace_bytes, lib.kda_bwd_workspace_bytes):
+        fn.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32, c_uint32]
+        fn.restype = c_size_t
+    lib.kda_status_string.argtypes = [c_int32]
+    lib.kda_status_string.restype = c_char_p
+    lib.kda_abi_version.argtypes = []
+    lib.kda_abi_version.restype = c_int32
+    lib.kda_launch_count.argtypes = []
+    lib.kda_launch_count.restype = ctypes.c_uint64
+    ver = lib.kda_abi_version()
+    if ver != ABI_VERSION:
+        raise ImportError(f"KDA library ABI version {ver} != binding version {ABI_VERSION}; rebuild")
+    _LIB = lib
+    return lib
+
+
+def status_string(code: int) -> str:
+    return load().kda_status_string(int(code)).decode()
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process."""
+    return int(load().kda_launch_count())

@@ -1,0 +1,172 @@
+// C-ABI entry points: argument validation and kernel dispatch.
+//
+// Mirrors the checks SimpleTrain's dispatch relies on (kernels/kda_kernel.py:
+// the Triton wrapper's dtype assert at :204, the head-dim cap at :216-219 and
+// the broadcast failure of the literal state update at :294-295) but reports
+// them as status codes instead of exceptions or silent fallbacks.
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "kda_internal.h"
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
+
+void kda::count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+namespace {
+
+using kda::View;
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_view(const kda_tensor &t, bool required) {
+  if (t.data == nullptr) return required ? KDA_ERR_NULL_ARGUMENT : KDA_OK;
+  if (t.stride_d != 1) return KDA_ERR_BAD_LAYOUT;
+  if (!aligned16(t.data)) return KDA_ERR_BAD_LAYOUT;
+  if ((t.stride_b % 8) || (t.stride_h % 8) || (t.stride_t % 8)) return KDA_ERR_BAD_LAYOUT;
+  if (t.stride_b < 0 || t.stride_h < 0 || t.stride_t < 0) return KDA_ERR_BAD_LAYOUT;
+  return KDA_OK;
+}
+
+View to_view(const kda_tensor &t) { return View{t.data, t.stride_b, t.stride_h, t.stride_t, t.stride_d}; }
+
+int check_common(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, int32_t dtype, uint32_t flags) {
+  if (B < 0 || H < 0 || T < 0 || D <= 0 || chunk <= 0) return KDA_ERR_BAD_SHAPE;
+  if (dtype != KDA_DTYPE_BF16 && dtype != KDA_DTYPE_F16) return KDA_ERR_UNSUPPORTED;
+  if (chunk != 64) return KDA_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return KDA_ERR_UNSUPPORTED;
+  if (flags & ~uint32_t(KDA_FLAG_LITERAL)) return KDA_ERR_UNSUPPORTED;
+  if ((flags & KDA_FLAG_LITERAL) && D != chunk) return KDA_ERR_BAD_SHAPE;
+  return KDA_OK;
+}
+
+kda::DecaySrc make_decay(const float *ptr, int64_t sb, int64_t sh, int64_t sd, double scalar, int T,
+                         int C) {
+  kda::DecaySrc s{};
+  s.ptr = ptr;
+  s.sb = sb;
+  s.sh = sh;
+  s.sd = sd;
+  s.scalar = scalar;
+  // python: (decay ** L) computed in double, then used as an fp32 scalar factor
+  s.alpha_full = (float)std::pow(scalar, (double)C);
+  s.alpha_tail = (float)std::pow(scalar, (double)(T % C == 0 ? C : T % C));
+  return s;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? KDA_OK : KDA_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+int32_t kda_abi_version(void) { return KDA_ABI_VERSION; }
+
+uint64_t kda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char *kda_status_string(int32_t s) {
+  switch (s) {
+    case KDA_OK: return "ok";
+    case KDA_ERR_NULL_ARGUMENT: return "a required pointer argument is NULL";
+    case KDA_ERR_BAD_SHAPE: return "invalid shape (negative size, or literal mode with D != chunk)";
+    case KDA_ERR_UNSUPPORTED: return "unsupported configuration (head dim must be 64 or 128, chunk 64, dtype bf16/f16)";
+    case KDA_ERR_BAD_LAYOUT: return "bad layout (innermost stride must be 1, other strides multiples of 8 elements, base 16-byte aligned)";
+    case KDA_ERR_WORKSPACE: return "workspace missing or too small";
+    case KDA_ERR_CUDA: return "CUDA launch or runtime error";
+    case KDA_ERR_DEVICE_TIMEOUT: return "device-side bounded wait expired";
+    default: return "unknown kda status";
+  }
+}
+
+size_t kda_fwd_workspace_bytes(int32_t, int32_t, int32_t, int32_t, int32_t, uint32_t) { return 0; }
+
+size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t, int32_t D, int32_t, uint32_t) {
+  // forward-direction part of the decay gradient, [B*H*D] doubles
+  return (size_t)(B > 0 ? B : 0) * (size_t)(H > 0 ? H : 0) * (size_t)(D > 0 ? D : 0) * sizeof(double);
+}
+
+int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
+  if (p == nullptr) return KDA_ERR_NULL_ARGUMENT;
+  int rc = check_common(p->B, p->H, p->T, p->D, p->chunk, p->dtype, p->flags);
+  if (rc) return rc;
+  const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
+  if (literal && p->state_out && (p->T % p->chunk) != 0) return KDA_ERR_BAD_SHAPE;
+  if ((p->state_in && !aligned16(p->state_in)) || (p->state_out && !aligned16(p->state_out)))
+    return KDA_ERR_BAD_LAYOUT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->H == 0) return KDA_OK;  // nothing to read or write
+  if (p->T == 0) {
+    // empty sequence: the final state is the initial one
+    if (p->state_out) {
+      const size_t n = (size_t)p->B * p->H * p->D * p->D * sizeof(float);
+      cudaError_t e = p->state_in ? cudaMemcpyAsync(p->state_out, p->state_in, n, cudaMemcpyDeviceToDevice, st)
+                                  : cudaMemsetAsync(p->state_out, 0, n, st);
+      return cuda_status(e);
+    }
+    return KDA_OK;
+  }
+  if ((rc = check_view(p->q, true)) || (rc = check_view(p->k, true)) || (rc = check_view(p->v, true)) ||
+      (rc = check_view(p->g, false)) || (rc = check_view(p->y, true)))
+    return rc;
+  const size_t need = kda_fwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags);
+  if (need && (p->workspace == nullptr || p->workspace_bytes < need)) return KDA_ERR_WORKSPACE;
+  kda::FwdArgs a{};
+  a.B = p->B; a.H = p->H; a.T = p->T; a.D = p->D; a.C = p->chunk;
+  a.literal = literal ? 1 : 0;
+  a.q = to_view(p->q); a.k = to_view(p->k); a.v = to_view(p->v); a.g = to_view(p->g); a.y = to_view(p->y);
+  a.decay = make_decay(p->decay, p->decay_stride_b, p->decay_stride_h, p->decay_stride_d, p->decay_scalar,
+                       p->T, p->chunk);
+  a.s_in = p->state_in;
+  a.s_out = p->state_out;
+  a.status = p->status;
+  return cuda_status(kda::launch_fwd_simt(a, p->dtype, st));
+}
+
+int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
+  if (p == nullptr) return KDA_ERR_NULL_ARGUMENT;
+  int rc = check_common(p->B, p->H, p->T, p->D, p->chunk, p->dtype, p->flags);
+  if (rc) return rc;
+  const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
+  if (literal && (p->T % p->chunk) != 0 && p->dstate_out) return KDA_ERR_BAD_SHAPE;
+  const bool gate = p->g.data != nullptr;
+  if (p->ddecay && p->dstate_out && p->state_out == nullptr) return KDA_ERR_NULL_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->H == 0) return KDA_OK;
+  if (p->T == 0) {
+    const size_t n = (size_t)p->B * p->H * p->D * p->D * sizeof(float);
+    cudaError_t e = cudaSuccess;
+    if (p->dstate_in)
+      e = p->dstate_out ? cudaMemcpyAsync(p->dstate_in, p->dstate_out, n, cudaMemcpyDeviceToDevice, st)
+                        : cudaMemsetAsync(p->dstate_in, 0, n, st);
+    if (e == cudaSuccess && p->ddecay)
+      e = cudaMemsetAsync(p->ddecay, 0, (size_t)p->B * p->H * p->D * sizeof(float), st);
+    return cuda_status(e);
+  }
+  if ((rc = check_view(p->q, true)) || (rc = check_view(p->k, true)) || (rc = check_view(p->v, true)) ||
+      (rc = check_view(p->g, false)) || (rc = check_view(p->dy, true)) || (rc = check_view(p->dq, true)) ||
+      (rc = check_view(p->dk, true)) || (rc = check_view(p->dv, true)) || (rc = check_view(p->dg, gate)))
+    return rc;
+  const size_t need = p->ddecay ? kda_bwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags) : 0;
+  if (need && (p->workspace == nullptr || p->workspace_bytes < need)) return KDA_ERR_WORKSPACE;
+  kda::BwdArgs a{};
+  a.B = p->B; a.H = p->H; a.T = p->T; a.D = p->D; a.C = p->chunk;
+  a.literal = literal ? 1 : 0;
+  a.q = to_view(p->q); a.k = to_view(p->k); a.v = to_view(p->v); a.g = to_view(p->g); a.dy = to_view(p->dy);
+  a.dq = to_view(p->dq); a.dk = to_view(p->dk); a.dv = to_view(p->dv); a.dg = to_view(p->dg);
+  a.decay = make_decay(p->decay, p->decay_stride_b, p->decay_stride_h, p->decay_stride_d, p->decay_scalar,
+                       p->T, p->chunk);
+  a.s_in = p->state_in;
+  a.s_out = p->state_out;
+  a.ds_out = p->dstate_out;
+  a.ds_in = p->dstate_in;
+  a.ddecay = p->ddecay;
+  a.sink = reinterpret_cast<double *>(p->workspace);
+  a.status = p->status;
+  return cuda_status(kda::launch_bwd_simt(a, p->dtype, st));
+}
+
+}  // extern "C"

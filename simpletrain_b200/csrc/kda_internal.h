@@ -1,0 +1,71 @@
+// Internal launch arguments shared by the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/kda_sm100.h"
+
+namespace kda {
+
+// One [B,H,T,D] view (element strides).
+struct View {
+  void *data;
+  int64_t sb, sh, st, sd;
+};
+
+// Per-channel chunk decay source.  alpha for a chunk of length L is
+//   decay**L  (tensor decay: powf in-kernel; scalar: host-computed in double,
+//   rounded once to fp32, matching `python_float ** L * fp32_state`).
+struct DecaySrc {
+  const float *ptr;  // nullptr -> scalar
+  int64_t sb, sh, sd;
+  float alpha_full;  // scalar decay**chunk
+  float alpha_tail;  // scalar decay**(T % chunk) (unused when T % chunk == 0)
+  double scalar;
+};
+
+struct FwdArgs {
+  int B, H, T, D, C;
+  int literal;
+  View q, k, v, g, y;  // g.data == nullptr -> no gate
+  DecaySrc decay;
+  const float *s_in;
+  float *s_out;
+  int32_t *status;
+};
+
+struct BwdArgs {
+  int B, H, T, D, C;
+  int literal;
+  View q, k, v, g, dy, dq, dk, dv, dg;
+  DecaySrc decay;
+  const float *s_in;
+  const float *s_out;
+  const float *ds_out;
+  float *ds_in;
+  float *ddecay;
+  double *sink;  // workspace [B*H*D] (decay gradient, forward-direction part)
+  int32_t *status;
+};
+
+// Device-side alpha for channel d of (b, h) and a chunk of length L.
+__device__ __forceinline__ float chunk_alpha(const DecaySrc &s, int b, int h, int d, int L, int C) {
+  if (s.ptr == nullptr) return (L == C) ? s.alpha_full : s.alpha_tail;
+  const float a = s.ptr[b * s.sb + h * s.sh + d * s.sd];
+  return powf(a, (float)L);
+}
+
+__device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, int d) {
+  if (s.ptr == nullptr) return (float)s.scalar;
+  return s.ptr[b * s.sb + h * s.sh + d * s.sd];
+}
+
+// Counts kernel launches for kda_launch_count().
+void count_launches(int n);
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_fwd_simt(const FwdArgs &a, int dtype, cudaStream_t st);
+cudaError_t launch_bwd_simt(const BwdArgs &a, int dtype, cudaStream_t st);
+
+}  // namespace kda

@@ -1,0 +1,119 @@
+"""Drop-in for SimpleTrain's ``kernels/kda_kernel.py``.
+
+Same public names and argument meaning as the reference module:
+
+* ``kda_chunked_scan(q, k, v, gate=None, decay=0.99, chunk_size=64,
+  use_triton=True) -> y``                      (``kernels/kda_kernel.py:303-328``)
+* ``kda_chunked_scan_triton(q, k, v, gate=None, decay=0.99, chunk_size=64)``
+                                               (``kernels/kda_kernel.py:195-238``)
+* ``_supported_arch()``                        (``kernels/kda_kernel.py:58-67``)
+
+Both scan functions run the sm_100a kernels through the ``kda_b200`` custom
+op; ``use_triton`` is accepted and ignored (there is one implementation and no
+fallback).  The result keeps the reference's conventions: y has q's dtype,
+shape and memory order (``:263``), the state is not returned (``:297``), and
+``decay`` is a float or a tensor broadcasting as ``[B, H, D, 1]`` against the
+state (``:295``).
+
+State-update semantics (module attribute ``SEMANTICS``, or the environment
+variable ``KDA_B200_SEMANTICS`` read at import):
+
+* ``"auto"`` (default) -- the reference's literal ``K V^T`` update
+  (``:294``) wherever the reference itself runs (D == chunk_size, and every
+  chunk but the last full or the last of length 1), so results match the
+  reference on those shapes; the ``K^T V`` update everywhere else (D=128,
+  where the reference raises).
+* ``"literal"`` -- always the reference's update; raises like the reference
+  (``RuntimeError``, same message) when D != chunk_size.
+* ``"corrected"`` -- always ``K^T V``.
+
+Errors: non-fp16/bf16 inputs raise ``AssertionError`` (the reference's
+Triton wrapper asserts the same, ``:204``); CPU tensors raise
+``RuntimeError`` (there is no CPU path).
+
+``install()`` makes ``import kernels.kda_kernel`` (and an already imported
+``models.kimi_k3``) resolve to this module, so ``models/kimi_k3.py`` and
+``train.py`` run unchanged.
+"""
+from __future__ import annotations
+
+import os
+import sys
+from typing import Optional, Union
+
+import torch
+
+from .ops import _validate, kda_chunk
+
+SEMANTICS = os.environ.get("KDA_B200_SEMANTICS", "auto")
+
+
+def _supported_arch() -> bool:
+    """True iff the current CUDA device is a B200-class sm_100 part."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        return torch.cuda.get_device_capability() == (10, 0)
+    except Exception:
+        return False
+
+
+def _use_literal(D: int, T: int, chunk_size: int) -> bool:
+    mode = SEMANTICS
+    if mode == "literal":
+        return True
+    if mode == "corrected":
+        return False
+    if mode != "auto":
+        raise ValueError(f"SEMANTICS must be 'auto', 'literal' or 'corrected', got {mode!r}")
+    return D == chunk_size and (T % chunk_size) in (0, 1)
+
+
+def _decay_arg(decay: Union[float, torch.Tensor], B: int, H: int, D: int):
+    """The reference's decay broadcast ([B, H, D, 1] against the state) as [B, H, D]."""
+    if not torch.is_tensor(decay):
+        return float(decay)
+    d = decay.float()
+    if d.dim() == 0:
+        return d.expand(B, H, D)
+    if d.shape[-1] != 1 and D != 1:
+        raise NotImplementedError(
+            "decay tensors must broadcast as [B, H, D, 1] (one factor per key-channel row)")
+    return torch.broadcast_to(d, (B, H, D, 1)).squeeze(-1)
+
+
+def kda_chunked_scan_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            gate: Optional[torch.Tensor] = None, decay: float = 0.99,
+                            chunk_size: int = 64) -> torch.Tensor:
+    """Run the scan on the sm_100a kernels; returns y of shape ``[B, H, T, D]``."""
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise AssertionError("KDA sm_100a kernel requires fp16/bf16")
+    _validate(q, k, v, gate, chunk_size)
+    B, H, T, D = q.shape
+    literal = _use_literal(D, T, chunk_size)
+    y, _ = kda_chunk(q, k, v, gate, _decay_arg(decay, B, H, D), None, chunk_size,
+                     reference_exact=literal, output_final_state=False)
+    return y
+
+
+def kda_chunked_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     gate: Optional[torch.Tensor] = None, decay: float = 0.99,
+                     chunk_size: int = 64, use_triton: bool = True) -> torch.Tensor:
+    """SimpleTrain's KDA dispatch, served by the sm_100a kernels (``use_triton`` ignored)."""
+    return kda_chunked_scan_triton(q, k, v, gate, decay, chunk_size)
+
+
+def install() -> None:
+    """Route SimpleTrain's ``kernels.kda_kernel`` imports to this module.
+
+    Call before importing ``models.kimi_k3``; an already imported
+    ``models.kimi_k3`` has its ``kda_chunked_scan`` name rebound too.
+    """
+    me = sys.modules[__name__]
+    sys.modules["kernels.kda_kernel"] = me
+    pkg = sys.modules.get("kernels")
+    if pkg is not None:
+        setattr(pkg, "kda_kernel", me)
+    model = sys.modules.get("models.kimi_k3")
+    if model is not None:
+        setattr(model, "kda_chunked_scan", kda_chunked_scan)

@@ -1,0 +1,270 @@
+"""torch.library custom ops over the sm_100a KDA C ABI, with autograd.
+
+``kda_b200::chunk_fwd`` and ``kda_b200::chunk_bwd`` call ``kda_fwd_sm100`` /
+``kda_bwd_sm100`` (``include/kda_sm100.h``) on torch's current CUDA stream,
+with outputs and workspace from the caching allocator, so they can be captured
+in CUDA graphs and traced by ``torch.compile`` (fake implementations are
+registered).  A nonzero ABI status raises ``RuntimeError``.  There is no CPU
+or fallback path: CPU tensors are rejected.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional, Tuple, Union
+
+import torch
+
+from . import _ffi
+
+Tensor = torch.Tensor
+
+_DTYPES = {torch.bfloat16: _ffi.KDA_DTYPE_BF16, torch.float16: _ffi.KDA_DTYPE_F16}
+_STATUS: Dict[int, Tensor] = {}
+
+
+def _lib():
+    return _ffi.load()
+
+
+def status_word(device: torch.device) -> Tensor:
+    """Per-device int32 word the kernels OR device-side error bits into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _STATUS.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = w
+    return w
+
+
+def device_status(device: Union[torch.device, int, None] = None, reset: bool = True) -> int:
+    """Read (and by default clear) the device-side error bits.  Synchronises."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    w = status_word(device)
+    val = int(w.item())
+    if reset and val:
+        w.zero_()
+    return val
+
+
+def _abi_layout_ok(t: Tensor) -> bool:
+    if t.stride(-1) != 1 and t.shape[-1] != 1:
+        return False
+    if t.data_ptr() % 16:
+        return False
+    return all(s % 8 == 0 for n, s in zip(t.shape[:-1], t.stride()[:-1]) if n != 1)
+
+
+def _prep(t: Optional[Tensor]) -> Optional[Tensor]:
+    if t is None:
+        return None
+    return t if _abi_layout_ok(t) else t.contiguous()
+
+
+def _desc(t: Optional[Tensor]) -> _ffi.KdaTensor:
+    if t is None:
+        return _ffi.KdaTensor(None, 0, 0, 0, 0)
+    st = [0 if n == 1 else s for n, s in zip(t.shape, t.stride())]
+    st[3] = 1
+    return _ffi.KdaTensor(t.data_ptr(), *st)
+
+
+def _ptr(t: Optional[Tensor]):
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _decay_fields(decay: Optional[Tensor]):
+    if decay is None:
+        return None, 0, 0, 0
+    st = [0 if n == 1 else s for n, s in zip(decay.shape, decay.stride())]
+    return decay.data_ptr(), st[0], st[1], st[2]
+
+
+def _check(rc: int, what: str):
+    if rc != _ffi.KDA_OK:
+        raise RuntimeError(f"{what} failed: {_ffi.status_string(rc)} (status {rc})")
+
+
+def _validate(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], chunk: int):
+    if q.device.type != "cuda":
+        raise RuntimeError("the KDA sm_100a kernels need CUDA tensors (there is no CPU path)")
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B, H, T, D], got shape {tuple(q.shape)}")
+    for n, t in (("k", k), ("v", v), ("gate", g)):
+        if t is None:
+            continue
+        if t.shape != q.shape:
+            raise ValueError(f"{n} shape {tuple(t.shape)} != q shape {tuple(q.shape)}")
+        if t.dtype != q.dtype or t.device != q.device:
+            raise TypeError(f"{n} must match q's dtype and device")
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"KDA sm_100a kernels take bf16/fp16 inputs, got {q.dtype}")
+
+
+# --------------------------------------------------------------------------- #
+# forward op
+# --------------------------------------------------------------------------- #
+@torch.library.custom_op("kda_b200::chunk_fwd", mutates_args=())
+def chunk_fwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], decay: Optional[Tensor],
+              decay_scalar: float, s0: Optional[Tensor], chunk: int, literal: bool,
+              want_state: bool) -> Tuple[Tensor, Tensor]:
+    q, k, v, g = _prep(q), _prep(k), _prep(v), _prep(g)
+    B, H, T, D = q.shape
+    y = torch.empty_like(q)               # like the reference (:263): keeps q's memory order
+    y = _prep(y)
+    s_out = (torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) if want_state
+             else torch.empty(0, dtype=torch.float32, device=q.device))
+    s_in = s0.contiguous().float() if s0 is not None else None
+    lib = _lib()
+    flags = _ffi.KDA_FLAG_LITERAL if literal else 0
+    ws_bytes = lib.kda_fwd_workspace_bytes(B, H, T, D, chunk, flags)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    dptr, dsb, dsh, dsd = _decay_fields(decay)
+    p = _ffi.KdaFwdParams(
+        B, H, T, D, chunk, _DTYPES[q.dtype], flags,
+        _desc(q), _desc(k), _desc(v), _desc(g), _desc(y),
+        dptr, dsb, dsh, dsd, float(decay_scalar),
+        _ptr(s_in), _ptr(s_out) if want_state else None,
+        _ptr(ws), ws_bytes, status_word(q.device).data_ptr(),
+    )
+    rc = lib.kda_fwd_sm100(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream))
+    _check(rc, "kda_fwd_sm100")
+    return y, s_out
+
+
+@chunk_fwd.register_fake
+def _(q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state):
+    B, H, T, D = q.shape
+    shape = (B, H, D, D) if want_state else (0,)
+    return torch.empty_like(q), q.new_empty(shape, dtype=torch.float32)
+
+
+# --------------------------------------------------------------------------- #
+# backward op
+# --------------------------------------------------------------------------- #
+@torch.library.custom_op("kda_b200::chunk_bwd", mutates_args=())
+def chunk_bwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], dy: Tensor,
+              decay: Optional[Tensor], decay_scalar: float, s0: Optional[Tensor],
+              s_T: Optional[Tensor], ds_T: Optional[Tensor], chunk: int, literal: bool,
+              need_ddecay: bool, need_ds0: bool
+              ) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    q, k, v, g, dy = _prep(q), _prep(k), _prep(v), _prep(g), _prep(dy)
+    B, H, T, D = q.shape
+    dev = q.device
+    dq, dk, dv = _prep(torch.empty_like(q)), _prep(torch.empty_like(k)), _prep(torch.empty_like(v))
+    dg = _prep(torch.empty_like(g)) if g is not None else torch.empty(0, dtype=q.dtype, device=dev)
+    need_ddecay = bool(need_ddecay and decay is not None)
+    ddecay = (torch.empty(B, H, D, dtype=torch.float32, device=dev) if need_ddecay
+              else torch.empty(0, dtype=torch.float32, device=dev))
+    ds0 = (torch.empty(B, H, D, D, dtype=torch.float32, device=dev) if need_ds0
+           else torch.empty(0, dtype=torch.float32, device=dev))
+    s_in = s0.contiguous().float() if s0 is not None else None
+    sT = s_T.contiguous() if (s_T is not None and s_T.numel()) else None
+    dsT = ds_T.contiguous().float() if (ds_T is not None and ds_T.numel()) else None
+    lib = _lib()
+    flags = _ffi.KDA_FLAG_LITERAL if literal else 0
+    ws_bytes = lib.kda_bwd_workspace_bytes(B, H, T, D, chunk, flags) if need_ddecay else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    dptr, dsb, dsh, dsd = _decay_fields(decay)
+    p = _ffi.KdaBwdParams(
+        B, H, T, D, chunk, _DTYPES[q.dtype], flags,
+        _desc(q), _desc(k), _desc(v), _desc(g), _desc(dy),
+        _desc(dq), _desc(dk), _desc(dv), _desc(dg if g is not None else None),
+        dptr, dsb, dsh, dsd, float(decay_scalar),
+        _ptr(s_in), _ptr(sT), _ptr(dsT),
+        _ptr(ds0) if need_ds0 else None, _ptr(ddecay) if need_ddecay else None,
+        _ptr(ws), ws_bytes, status_word(dev).data_ptr(),
+    )
+    rc = lib.kda_bwd_sm100(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    _check(rc, "kda_bwd_sm100")
+    return dq, dk, dv, dg, ddecay, ds0
+
+
+@chunk_bwd.register_fake
+def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, literal, need_ddecay, need_ds0):
+    B, H, T, D = q.shape
+    f32 = torch.float32
+    dg = torch.empty_like(g) if g is not None else q.new_empty((0,))
+    dd = q.new_empty((B, H, D) if (need_ddecay and decay is not None) else (0,), dtype=f32)
+    ds0 = q.new_empty((B, H, D, D) if need_ds0 else (0,), dtype=f32)
+    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), dg, dd, ds0
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state = inputs
+    y, s_T = output
+    ctx.save_for_backward(q, k, v, g, decay, s0, s_T if want_state else None)
+    ctx.decay_scalar = decay_scalar
+    ctx.chunk = chunk
+    ctx.literal = literal
+    ctx.has_gate = g is not None
+
+
+def _backward(ctx, dy, ds_T):
+    q, k, v, g, decay, s0, s_T = ctx.saved_tensors
+    need = ctx.needs_input_grad
+    need_ddecay = bool(need[4]) and decay is not None
+    need_ds0 = bool(need[6]) and s0 is not None
+    if dy is None:
+        dy = torch.zeros_like(q)
+    use_dsT = ds_T is not None and ds_T.numel() > 0 and s_T is not None
+    dq, dk, dv, dg, ddecay, ds0 = torch.ops.kda_b200.chunk_bwd(
+        q, k, v, g, dy, decay, ctx.decay_scalar, s0,
+        s_T if use_dsT else None, ds_T if use_dsT else None,
+        ctx.chunk, ctx.literal, need_ddecay, need_ds0)
+    return (dq, dk, dv, dg if ctx.has_gate else None,
+            ddecay if need_ddecay else None, None,
+            ds0 if need_ds0 else None, None, None, None)
+
+
+torch.library.register_autograd("kda_b200::chunk_fwd", _backward, setup_context=_setup_context)
+
+
+# --------------------------------------------------------------------------- #
+# extended public API
+# --------------------------------------------------------------------------- #
+def decay_as_bhd(decay: Union[float, Tensor], B: int, H: int, D: int) -> Tuple[Optional[Tensor], float]:
+    """Normalise the extended API's decay to (fp32 [B,H,D] view or None, scalar).
+
+    Accepted: a Python float; a tensor of shape (), (H,) (per head), (H, D)
+    (per key channel), (B, H, D), or anything broadcastable to (B, H, D).
+    """
+    if not torch.is_tensor(decay):
+        return None, float(decay)
+    d = decay.float()
+    if d.dim() == 1 and d.shape[0] == H:
+        d = d.view(H, 1)
+    return torch.broadcast_to(d, (B, H, D)), 0.0
+
+
+def kda_chunk(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
+              decay: Union[float, Tensor] = 0.99, initial_state: Optional[Tensor] = None,
+              chunk_size: int = 64, reference_exact: bool = False,
+              output_final_state: bool = True) -> Tuple[Tensor, Optional[Tensor]]:
+    """KDA chunked scan on B200: returns ``(y, final_state)``.
+
+    q, k, v, g: ``[B, H, T, D]`` bf16/fp16 CUDA tensors (any strides; the
+    ``[B, T, H, D]``-memory views the KDA layer produces are used in place).
+    decay: float or tensor (see ``decay_as_bhd``); per chunk of length L the
+    state's key-channel rows are scaled by ``decay**L``.  initial_state:
+    ``[B, H, D, D]`` fp32 or None (zeros).  ``reference_exact`` selects the
+    reference's literal ``K V^T`` state update (``kernels/kda_kernel.py:294``,
+    needs D == chunk_size); the default is the ``K^T V`` form.  Differentiable
+    in q, k, v, g, a tensor decay and the initial state.
+    """
+    _validate(q, k, v, g, chunk_size)
+    B, H, T, D = q.shape
+    if reference_exact and D != chunk_size:
+        raise RuntimeError(
+            f"The size of tensor a ({D}) must match the size of tensor b ({chunk_size}) "
+            f"at non-singleton dimension 3")
+    if reference_exact and output_final_state and T % chunk_size:
+        raise ValueError("reference_exact: the final state of a ragged last chunk is not defined")
+    dt, ds = decay_as_bhd(decay, B, H, D)
+    if initial_state is not None and initial_state.shape != (B, H, D, D):
+        raise ValueError(f"initial_state must be [B, H, D, D] = {(B, H, D, D)}")
+    y, s = torch.ops.kda_b200.chunk_fwd(q, k, v, g, dt, ds, initial_state, int(chunk_size),
+                                        bool(reference_exact), bool(output_final_state))
+    return y, (s if output_final_state else None)

@@ -1,0 +1,125 @@
+"""The C ABI library: loads, exports what include/kda_sm100.h declares, and
+the ctypes mirror has the C layout.  No kernel launches (runs without a GPU)."""
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+import tempfile
+
+import pytest
+
+from simpletrain_b200 import _ffi
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+HEADER = os.path.join(ROOT, "include", "kda_sm100.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(kda_[a-z0-9_]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _ffi.load()
+    declared = _declared_functions()
+    assert set(declared) >= set(_ffi.EXPORTED), declared
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert lib.kda_abi_version() == _ffi.ABI_VERSION
+
+
+def test_nm_shows_c_linkage():
+    if shutil.which("nm") is None:
+        pytest.skip("nm not available")
+    out = subprocess.run(["nm", "-D", "--defined-only", _ffi.LIB_PATH], capture_output=True, text=True).stdout
+    for name in _declared_functions():
+        assert re.search(rf"\bT {name}$", out, flags=re.M), name
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_ctypes_structs_match_c_layout():
+    probe = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "kda_sm100.h"
+#define F(s, m) printf(#s "." #m " %zu\n", offsetof(s, m));
+int main(void) {
+  printf("kda_tensor %zu\nkda_fwd_params %zu\nkda_bwd_params %zu\n",
+         sizeof(kda_tensor), sizeof(kda_fwd_params), sizeof(kda_bwd_params));
+  F(kda_fwd_params, q) F(kda_fwd_params, y) F(kda_fwd_params, decay) F(kda_fwd_params, decay_scalar)
+  F(kda_fwd_params, state_in) F(kda_fwd_params, workspace_bytes) F(kda_fwd_params, status)
+  F(kda_bwd_params, q) F(kda_bwd_params, dg) F(kda_bwd_params, decay) F(kda_bwd_params, decay_scalar)
+  F(kda_bwd_params, dstate_out) F(kda_bwd_params, ddecay) F(kda_bwd_params, status)
+  return 0;
+}
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "probe.c")
+        exe = os.path.join(d, "probe")
+        open(c, "w").write(probe)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        lines = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = dict(l.rsplit(" ", 1) for l in lines if l)
+    assert int(got["kda_tensor"]) == ctypes.sizeof(_ffi.KdaTensor)
+    assert int(got["kda_fwd_params"]) == ctypes.sizeof(_ffi.KdaFwdParams)
+    assert int(got["kda_bwd_params"]) == ctypes.sizeof(_ffi.KdaBwdParams)
+    for key, val in got.items():
+        if "." in key:
+            sname, field = key.split(".")
+            cls = {"kda_fwd_params": _ffi.KdaFwdParams, "kda_bwd_params": _ffi.KdaBwdParams}[sname]
+            assert getattr(cls, field).offset == int(val), key
+
+
+def _fwd_params(**kw):
+    p = _ffi.KdaFwdParams()
+    p.B, p.H, p.T, p.D, p.chunk, p.dtype = 1, 1, 64, 64, 64, _ffi.KDA_DTYPE_BF16
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(D=96), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(chunk=32), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(dtype=7), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(flags=1 << 5), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(T=-1), _ffi.KDA_ERR_BAD_SHAPE),
+    (dict(D=128, flags=_ffi.KDA_FLAG_LITERAL), _ffi.KDA_ERR_BAD_SHAPE),
+    (dict(B=0), _ffi.KDA_OK),       # empty batch: nothing to do, no pointers touched
+    (dict(H=0), _ffi.KDA_OK),
+])
+def test_forward_argument_checks(kw, code):
+    lib = _ffi.load()
+    assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params(**kw)), None) == code
+
+
+def test_null_params_and_missing_tensors():
+    lib = _ffi.load()
+    assert lib.kda_fwd_sm100(None, None) == _ffi.KDA_ERR_NULL_ARGUMENT
+    assert lib.kda_bwd_sm100(None, None) == _ffi.KDA_ERR_NULL_ARGUMENT
+    # q is NULL while there is work to do
+    assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params()), None) == _ffi.KDA_ERR_NULL_ARGUMENT
+
+
+def test_layout_rules_are_enforced_before_any_launch():
+    lib = _ffi.load()
+    good = _ffi.KdaTensor(0x10000, 64 * 64, 64 * 64, 64, 1)
+    p = _fwd_params(q=good, k=good, v=good, y=good)
+    p.q = _ffi.KdaTensor(0x10000, 64 * 64, 64 * 64, 64, 2)      # strided innermost dim
+    assert lib.kda_fwd_sm100(ctypes.byref(p), None) == _ffi.KDA_ERR_BAD_LAYOUT
+    p.q = _ffi.KdaTensor(0x10008, 64 * 64, 64 * 64, 64, 1)      # 8-byte aligned base
+    assert lib.kda_fwd_sm100(ctypes.byref(p), None) == _ffi.KDA_ERR_BAD_LAYOUT
+    p.q = _ffi.KdaTensor(0x10000, 64 * 64, 64 * 64, 65, 1)      # token stride not 16-byte multiple
+    assert lib.kda_fwd_sm100(ctypes.byref(p), None) == _ffi.KDA_ERR_BAD_LAYOUT
+
+
+def test_workspace_sizes_and_status_strings():
+    lib = _ffi.load()
+    assert lib.kda_bwd_workspace_bytes(2, 3, 128, 64, 64, 0) >= 2 * 3 * 64 * 8
+    for code in (0, 1, 2, 3, 4, 5, 6, 64):
+        s = _ffi.status_string(code)
+        assert s and s != "unknown kda status"
+    assert _ffi.status_string(12345) == "unknown kda status"
