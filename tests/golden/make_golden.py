@@ -14,7 +14,8 @@ records the error it raises instead.
 
 Fixtures (``tests/golden/*.pt``):
   lit_f32.pt        B1 H2 T128 D64, fp32, gate, float decay 0.93; y + grads q,k,v,g
-  lit_bf16.pt       B1 H2 T128 D64, bf16, gate, tensor decay [1,H,D,1]; y + grads incl. decay
+  lit_bf16.pt       B1 H2 T192 D64, bf16, gate, tensor decay [1,H,D,1]; y + grads incl. decay
+                    (three chunks, so the decay reaches the output through the state)
   lit_tail1.pt      B1 H1 T129 D64, fp32, no gate, float decay (1-token tail chunk)
   cpu_fwd_f32.pt    the seeded CPU workload (B2 H8 T512 D64 fp32, seed 0) with
                     decay = mean of the drawn per-channel decays: input checksums,
@@ -78,7 +79,7 @@ def main():
                os.path.join(HERE, "lit_f32.pt"))
 
     # 2) literal bf16 with tensor decay [1,H,D,1] (autograd gives its gradient)
-    q, k, v, gt, dy = _inputs(1, 2, 128, 64, torch.bfloat16, 12)
+    q, k, v, gt, dy = _inputs(1, 2, 192, 64, torch.bfloat16, 12)
     decay = torch.sigmoid(torch.randn(1, 2, 64, 1, generator=torch.Generator().manual_seed(13)) + 3.0)
     res = _run(ref, q, k, v, gt, dy, decay, 64)
     torch.save({"q": q, "k": k, "v": v, "g": gt, "dy": dy, "decay": decay, "chunk": 64, **res},

@@ -184,6 +184,18 @@ def test_dropin_matches_reference_golden_bf16(golden_dir):
         assert e <= TOL_LOWP, (name, e)
 
 
+def test_decay_gradient_vanishes_when_decay_only_scales_zero_state():
+    """Two chunks from a zero state: decay multiplies only the zero initial state
+    and the unused final update, so d(loss)/d(decay) is exactly 0 in the
+    reference; the closed form returns rounding noise far below the terms."""
+    q, k, v, g, dy, dch = _rand(1, 2, 128, 64, seed=5)
+    dl = dch.to(DEV).requires_grad_(True)
+    y, _ = kda_chunk(q.to(DEV), k.to(DEV), v.to(DEV), g.to(DEV), dl, None, 64,
+                     reference_exact=True, output_final_state=False)
+    (y.float() * dy.to(DEV).float()).sum().backward()
+    assert dl.grad.abs().max().item() < 1e-3
+
+
 def test_dropin_matches_reference_golden_f32_inputs_cast(golden_dir):
     f = torch.load(os.path.join(golden_dir, "lit_f32.pt"), weights_only=False)
     cast = lambda t: t.to(DEV, torch.bfloat16)
