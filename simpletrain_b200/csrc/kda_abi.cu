@@ -123,7 +123,7 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   a.s_in = p->state_in;
   a.s_out = p->state_out;
   a.status = p->status;
-  return cuda_status(kda::launch_fwd_simt(a, p->dtype, st));
+  return cuda_status(kda::launch_fwd_tc(a, p->dtype, st));
 }
 
 int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {

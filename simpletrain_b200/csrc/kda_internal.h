@@ -66,6 +66,7 @@ void count_launches(int n);
 
 // Launchers (return cudaError_t of the launch).
 cudaError_t launch_fwd_simt(const FwdArgs &a, int dtype, cudaStream_t st);
+cudaError_t launch_fwd_tc(const FwdArgs &a, int dtype, cudaStream_t st);
 cudaError_t launch_bwd_simt(const BwdArgs &a, int dtype, cudaStream_t st);
 
 }  // namespace kda
