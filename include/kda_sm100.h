@@ -103,11 +103,10 @@ typedef struct kda_bwd_params {
   int64_t decay_stride_b, decay_stride_h, decay_stride_d;
   double decay_scalar;
   const float *state_in;   /* forward's initial state, NULL -> zeros */
-  const float *state_out;  /* forward's final state; required when dstate_out and ddecay are both set */
   const float *dstate_out; /* dL/d(final state), NULL -> zero */
   float *dstate_in;        /* out: dL/d(initial state), NULL -> not written */
   float *ddecay;           /* out: [B,H,D] fp32 dL/d(decay[b,h,d]), NULL -> not computed */
-  void *workspace;
+  void *workspace;         /* kda_bwd_workspace_bytes() bytes, 256-byte aligned */
   size_t workspace_bytes;
   int32_t *status;
 } kda_bwd_params;

@@ -37,7 +37,7 @@ channel), which the reference's ``decay ** L * state`` also accepts.
 The extensions over the reference (an initial state, the returned final state)
 are plain additions to the same loop.  ``manual_backward`` restates, in
 float64, the two-direction backward that the CUDA kernels implement, including
-the closed-form decay gradient, so the algorithm itself is checked against
+the forward-mode decay gradient, so the algorithm itself is checked against
 autograd on the CPU.
 """
 from __future__ import annotations
@@ -164,22 +164,22 @@ def naive_recurrence(q, k, v, gate, decay: float, chunk_size: int,
 def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
                     initial_state: Optional[torch.Tensor], dy: torch.Tensor,
                     dstate_T: Optional[torch.Tensor] = None, mode: str = "corrected"):
-    """Explicit chunk backward in float64.
+    """Explicit chunk backward in float64 -- the algorithm the CUDA kernels run.
 
     Gradients of  L = <dy, y> + <dstate_T, S_T>  for y, S_T = chunk_scan(...).
-    Forward-direction pass ("A") recomputes S_{c-1} chunk by chunk and gives
-    dq and dg; reverse pass ("B") carries dS and gives dk, dv and d(initial
-    state).  The decay gradient uses a closed form that needs no stored
-    states: with a[i] the per-channel decay and exponents counted in tokens,
+    The forward-direction pass ("A") recomputes S_{c-1} chunk by chunk and
+    gives dq, dg and the decay gradient; the reverse pass ("B") carries
+    dS_c = dL/dS_c and gives dk, dv and d(initial state).  Neither pass needs
+    the other's carry.
 
-        dL/dlog a[i] = sum_t start(c_t) q_t[i] dq_inter_t[i]
-                     - sum_c end(c) <dS_c[i,:], U_c[i,:]>
-                     + T <dS_T[i,:], S_T[i,:]>
+    Decay gradient, forward mode: the state's key-channel row i is scaled by
+    alpha_c[i] = a[i]**L_c, so its tangent T_c = dS_c/dlog a (row-wise) obeys
 
-    where dq_inter = dO S_{c-1}^T, U_c is the chunk's state update and dS_c
-    the gradient reaching S_c.  (Every state entry is a sum of sources
-    decayed by a^(start(sink) - end(source)); differentiating the exponent
-    splits into a sink part and a source part.)  Returns
+        T_c = alpha_c * (T_{c-1} + L_c * S_{c-1}),   T_{-1} = 0,
+
+    and  dL/dlog a[i] = sum_t q_t[i] (dO_t T_{c(t)-1}^T)[i] + <dS_T[i,:], T_T[i,:]>.
+    Every term is a product of actual quantities (no large terms cancel), so
+    the bf16 tensor-core operands do not limit its accuracy.  Returns
     (dq, dk, dv, dg, d_decay[B,H,D], d_initial_state).
     """
     B, H, T, D = q.shape
@@ -198,11 +198,11 @@ def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
 
     dq = torch.zeros_like(Q); dk = torch.zeros_like(K); dv = torch.zeros_like(V)
     dg = torch.zeros_like(Q) if G is not None else None
-    sink = torch.zeros(B, H, D, dtype=f)
-    source = torch.zeros(B, H, D, dtype=f)
+    dlog = torch.zeros(B, H, D, dtype=f)
 
-    # pass A: forward direction
+    # pass A: forward direction (S and its decay tangent Td)
     S = S0.clone()
+    Td = torch.zeros_like(S)
     for (t0, t1) in chunks:
         L = t1 - t0
         Qc, Kc, Vc, DYc = Q[:, :, t0:t1], K[:, :, t0:t1], V[:, :, t0:t1], DY[:, :, t0:t1]
@@ -214,11 +214,13 @@ def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
         else:
             dO = DYc
         dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
-        dq_inter = dO @ S.transpose(-1, -2)
-        dq[:, :, t0:t1] = dP @ Kc + dq_inter
-        sink += t0 * (Qc * dq_inter).sum(dim=2)
-        S = (a ** L).unsqueeze(-1) * S + update(Kc, Vc)
-    S_T = S
+        dq[:, :, t0:t1] = dP @ Kc + dO @ S.transpose(-1, -2)
+        dlog += (Qc * (dO @ Td.transpose(-1, -2))).sum(dim=2)
+        alpha = (a ** L).unsqueeze(-1)
+        Td = alpha * (Td + L * S)
+        S = alpha * S + update(Kc, Vc)
+    if dstate_T is not None:
+        dlog += (dstate_T.to(f) * Td).sum(dim=-1)
 
     # pass B: reverse direction
     dS = dstate_T.to(f).clone() if dstate_T is not None else torch.zeros(B, H, D, D, dtype=f)
@@ -231,18 +233,13 @@ def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
         if mode == "literal":
             dk_inter = dS @ Vc                     # d/dK of K V^T against dS
             dv_inter = dS.transpose(-1, -2) @ Kc
-            source += t1 * (Kc * dk_inter).sum(dim=-1)     # row i of K V^T is token i
         else:
             dk_inter = Vc @ dS.transpose(-1, -2)
             dv_inter = Kc @ dS
-            source += t1 * (Kc * dk_inter).sum(dim=2)
         dk[:, :, t0:t1] = dP.transpose(-1, -2) @ Qc + dk_inter
         dv[:, :, t0:t1] = P.transpose(-1, -2) @ dO + dv_inter
         dS = Qc.transpose(-1, -2) @ dO + (a ** L).unsqueeze(-1) * dS
     dS0 = dS
 
-    dlog = sink - source
-    if dstate_T is not None:
-        dlog = dlog + T * (dstate_T.to(f) * S_T).sum(dim=-1)
     d_decay = torch.where(a != 0, dlog / torch.where(a != 0, a, torch.ones_like(a)), torch.zeros_like(a))
     return dq, dk, dv, dg, d_decay, dS0

@@ -58,7 +58,7 @@ class KdaBwdParams(ctypes.Structure):
         ("dq", KdaTensor), ("dk", KdaTensor), ("dv", KdaTensor), ("dg", KdaTensor),
         ("decay", c_void_p), ("decay_stride_b", c_int64), ("decay_stride_h", c_int64),
         ("decay_stride_d", c_int64), ("decay_scalar", c_double),
-        ("state_in", c_void_p), ("state_out", c_void_p), ("dstate_out", c_void_p),
+        ("state_in", c_void_p), ("dstate_out", c_void_p),
         ("dstate_in", c_void_p), ("ddecay", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("status", c_void_p),

@@ -84,10 +84,7 @@ const char *kda_status_string(int32_t s) {
 
 size_t kda_fwd_workspace_bytes(int32_t, int32_t, int32_t, int32_t, int32_t, uint32_t) { return 0; }
 
-size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t, int32_t D, int32_t, uint32_t) {
-  // forward-direction part of the decay gradient, [B*H*D] doubles
-  return (size_t)(B > 0 ? B : 0) * (size_t)(H > 0 ? H : 0) * (size_t)(D > 0 ? D : 0) * sizeof(double);
-}
+size_t kda_bwd_workspace_bytes(int32_t, int32_t, int32_t, int32_t, int32_t, uint32_t) { return 0; }
 
 int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   if (p == nullptr) return KDA_ERR_NULL_ARGUMENT;
@@ -133,7 +130,6 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   if (literal && (p->T % p->chunk) != 0 && p->dstate_out) return KDA_ERR_BAD_SHAPE;
   const bool gate = p->g.data != nullptr;
-  if (p->ddecay && p->dstate_out && p->state_out == nullptr) return KDA_ERR_NULL_ARGUMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->H == 0) return KDA_OK;
   if (p->T == 0) {
@@ -150,7 +146,7 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
       (rc = check_view(p->g, false)) || (rc = check_view(p->dy, true)) || (rc = check_view(p->dq, true)) ||
       (rc = check_view(p->dk, true)) || (rc = check_view(p->dv, true)) || (rc = check_view(p->dg, gate)))
     return rc;
-  const size_t need = p->ddecay ? kda_bwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags) : 0;
+  const size_t need = kda_bwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags);
   if (need && (p->workspace == nullptr || p->workspace_bytes < need)) return KDA_ERR_WORKSPACE;
   kda::BwdArgs a{};
   a.B = p->B; a.H = p->H; a.T = p->T; a.D = p->D; a.C = p->chunk;
@@ -160,13 +156,11 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   a.decay = make_decay(p->decay, p->decay_stride_b, p->decay_stride_h, p->decay_stride_d, p->decay_scalar,
                        p->T, p->chunk);
   a.s_in = p->state_in;
-  a.s_out = p->state_out;
   a.ds_out = p->dstate_out;
   a.ds_in = p->dstate_in;
   a.ddecay = p->ddecay;
-  a.sink = reinterpret_cast<double *>(p->workspace);
   a.status = p->status;
-  return cuda_status(kda::launch_bwd_simt(a, p->dtype, st));
+  return cuda_status(kda::launch_bwd_tc(a, p->dtype, st));
 }
 
 }  // extern "C"

@@ -41,11 +41,9 @@ struct BwdArgs {
   View q, k, v, g, dy, dq, dk, dv, dg;
   DecaySrc decay;
   const float *s_in;
-  const float *s_out;
   const float *ds_out;
   float *ds_in;
   float *ddecay;
-  double *sink;  // workspace [B*H*D] (decay gradient, forward-direction part)
   int32_t *status;
 };
 
@@ -65,8 +63,7 @@ __device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, in
 void count_launches(int n);
 
 // Launchers (return cudaError_t of the launch).
-cudaError_t launch_fwd_simt(const FwdArgs &a, int dtype, cudaStream_t st);
 cudaError_t launch_fwd_tc(const FwdArgs &a, int dtype, cudaStream_t st);
-cudaError_t launch_bwd_simt(const BwdArgs &a, int dtype, cudaStream_t st);
+cudaError_t launch_bwd_tc(const BwdArgs &a, int dtype, cudaStream_t st);
 
 }  // namespace kda

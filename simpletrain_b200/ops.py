@@ -161,11 +161,10 @@ def chunk_bwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], dy: Tensor,
     ds0 = (torch.empty(B, H, D, D, dtype=torch.float32, device=dev) if need_ds0
            else torch.empty(0, dtype=torch.float32, device=dev))
     s_in = s0.contiguous().float() if s0 is not None else None
-    sT = s_T.contiguous() if (s_T is not None and s_T.numel()) else None
     dsT = ds_T.contiguous().float() if (ds_T is not None and ds_T.numel()) else None
     lib = _lib()
     flags = _ffi.KDA_FLAG_LITERAL if literal else 0
-    ws_bytes = lib.kda_bwd_workspace_bytes(B, H, T, D, chunk, flags) if need_ddecay else 0
+    ws_bytes = lib.kda_bwd_workspace_bytes(B, H, T, D, chunk, flags)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     dptr, dsb, dsh, dsd = _decay_fields(decay)
     p = _ffi.KdaBwdParams(
@@ -173,7 +172,7 @@ def chunk_bwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], dy: Tensor,
         _desc(q), _desc(k), _desc(v), _desc(g), _desc(dy),
         _desc(dq), _desc(dk), _desc(dv), _desc(dg if g is not None else None),
         dptr, dsb, dsh, dsd, float(decay_scalar),
-        _ptr(s_in), _ptr(sT), _ptr(dsT),
+        _ptr(s_in), _ptr(dsT),
         _ptr(ds0) if need_ds0 else None, _ptr(ddecay) if need_ddecay else None,
         _ptr(ws), ws_bytes, status_word(dev).data_ptr(),
     )

@@ -151,7 +151,7 @@ def test_gradcheck_corrected_float64():
 
 
 # --------------------------------------------------------------------------- #
-# the kernels' backward algorithm (incl. closed-form decay gradient) vs autograd
+# the kernels' backward algorithm (incl. forward-mode decay gradient) vs autograd
 # --------------------------------------------------------------------------- #
 @pytest.mark.parametrize("mode,D,T,gate,with_s0,with_dsT", [
     ("corrected", 16, 150, True, True, True),
