@@ -435,6 +435,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="1b-fwdbwd", choices=sorted(WORKLOADS))
+    ap.add_argument("--shape", default=None,
+                    help="B,H,T,D: run a custom shape (profiling / sweeps) instead of --workload")
+    ap.add_argument("--fwd-only", action="store_true", help="with --shape: forward pass only")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -446,6 +449,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     w = WORKLOADS[args.workload]
+    if args.shape:
+        from simpletrain_b200.workloads import custom
+        B, H, T, D = (int(x) for x in args.shape.split(","))
+        w = custom(B, H, T, D, backward=not args.fwd_only)
 
     if args.impl == "reference":
         out = run_reference(args, w, rank, world)
