@@ -62,8 +62,16 @@ __device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, in
 // Counts kernel launches for kda_launch_count().
 void count_launches(int n);
 
-// Launchers (return cudaError_t of the launch).
-cudaError_t launch_fwd_tc(const FwdArgs &a, int dtype, cudaStream_t st);
-cudaError_t launch_bwd_tc(const BwdArgs &a, int dtype, cudaStream_t st);
+namespace tc {
+struct Queue;
+}
+
+// Launchers (return cudaError_t of the launch).  `grid` persistent CTAs work
+// through the queue's units.
+cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dtype, cudaStream_t st);
+cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue &q2, int grid1, int grid2,
+                          int dtype, cudaStream_t st);
+// CTAs of the forward kernel that fit on one SM.
+int fwd_tc_occupancy(int D, int dtype, bool literal);
 
 }  // namespace kda
