@@ -133,6 +133,29 @@ int32_t kda_abi_version(void);
    (diagnostic; no counterpart in the reference). */
 uint64_t kda_launch_count(void);
 
+/* Size of the fixed device scratch array used by kda_fwd_sm100_noalloc. */
+#define KDA_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/* Forward scan that allocates nothing and takes no workspace (no counterpart
+   in the reference; an addition of this library).
+   For callers that cannot allocate device memory for a workspace -- e.g. a
+   host runtime that binds this ABI but only holds the tensors it was given,
+   or a process whose device memory is reserved up front.  Inputs, outputs and
+   results are exactly those of kda_fwd_sm100 (p->workspace and
+   p->workspace_bytes are ignored); the scratch comes from a file-scope device
+   array of KDA_NOALLOC_SCRATCH_BYTES that every GPU loading it holds until
+   the process exits.
+   - Returns KDA_ERR_WORKSPACE, before enqueuing anything, when the problem
+     needs more than KDA_NOALLOC_SCRATCH_BYTES of scratch
+     (kda_fwd_workspace_bytes() tells how much: 128 KiB per (batch, head) at
+     D=128, 32 KiB at D=64, plus a small header).
+   - The first call on a device looks up the array's device address; make that
+     first call before any stream capture.
+   - Calls share the array and it keeps the last call's contents; each call
+     clears what must start at zero on its own stream.  Calls that overlap on
+     the GPU race on the array: serialise them (one stream, or events). */
+int kda_fwd_sm100_noalloc(const kda_fwd_params *p, kda_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

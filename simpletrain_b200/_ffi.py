@@ -28,8 +28,9 @@ KDA_ERR_DEVICE_TIMEOUT = 64
 
 EXPORTED = (
     "kda_fwd_sm100", "kda_bwd_sm100", "kda_fwd_workspace_bytes", "kda_bwd_workspace_bytes",
-    "kda_status_string", "kda_abi_version", "kda_launch_count",
+    "kda_status_string", "kda_abi_version", "kda_launch_count", "kda_fwd_sm100_noalloc",
 )
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 
 class KdaTensor(ctypes.Structure):
@@ -91,6 +92,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.kda_abi_version.restype = c_int32
     lib.kda_launch_count.argtypes = []
     lib.kda_launch_count.restype = ctypes.c_uint64
+    lib.kda_fwd_sm100_noalloc.argtypes = [POINTER(KdaFwdParams), c_void_p]
+    lib.kda_fwd_sm100_noalloc.restype = c_int32
     ver = lib.kda_abi_version()
     if ver != ABI_VERSION:
         raise ImportError(f"KDA library ABI version {ver} != binding version {ABI_VERSION}; rebuild")

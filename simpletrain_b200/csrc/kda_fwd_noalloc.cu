@@ -1,0 +1,68 @@
+// kda_fwd_sm100_noalloc: the forward scan with its scratch in a fixed,
+// file-scope device array instead of a caller-provided workspace.
+//
+// Who needs it: callers that cannot allocate device memory for a workspace --
+// for instance a host runtime that binds this C ABI and only holds the tensors
+// it was handed (its allocator belongs to someone else), or a serving process
+// whose device memory is reserved up front and must not grow mid-run.  They
+// pass inputs and outputs as usual; the scratch (the work-queue counter, the
+// per-stream flags and the state handoff slots) comes from the array below.
+//
+// Cost and limits: every GPU that loads this module holds the array
+// (kKdaScratchBytes) until the process exits.  Problems whose scratch would
+// exceed it are rejected with KDA_ERR_WORKSPACE before anything is enqueued.
+// All calls share the array and it keeps the last call's contents: each call
+// clears the part that must start at zero (the queue header) on its stream,
+// and calls that overlap on the GPU (different streams, or different host
+// threads) race on it and must be serialised by the caller.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/kda_sm100.h"
+
+namespace {
+
+constexpr size_t kKdaScratchBytes = KDA_NOALLOC_SCRATCH_BYTES;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_kda_scratch[kKdaScratchBytes];
+
+struct DeviceScratch {
+  std::once_flag once;
+  void *ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+DeviceScratch g_scratch[kMaxDevices];
+
+// Device address of the array for the current device.  The first call on a
+// device looks it up (host code may not use the symbol itself: on the host it
+// names a stand-in object, not device memory).
+int scratch_for_current_device(void **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KDA_ERR_CUDA;
+  DeviceScratch &d = g_scratch[dev];
+  std::call_once(d.once, [&d] {
+    void *p = nullptr;
+    d.err = cudaGetSymbolAddress(&p, g_kda_scratch);
+    d.ptr = p;
+  });
+  if (d.err != cudaSuccess || d.ptr == nullptr) return KDA_ERR_CUDA;
+  *out = d.ptr;
+  return KDA_OK;
+}
+
+}  // namespace
+
+extern "C" int kda_fwd_sm100_noalloc(const kda_fwd_params *p, kda_stream_t stream) {
+  if (p == nullptr) return KDA_ERR_NULL_ARGUMENT;
+  const size_t need = kda_fwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags);
+  if (need > kKdaScratchBytes) return KDA_ERR_WORKSPACE;
+  void *scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != KDA_OK) return rc;
+  kda_fwd_params q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = kKdaScratchBytes;
+  return kda_fwd_sm100(&q, stream);
+}

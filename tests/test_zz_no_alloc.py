@@ -1,0 +1,84 @@
+"""kda_fwd_sm100_noalloc: the forward scan for callers that cannot allocate.
+
+Some callers of this C ABI cannot allocate device memory for a workspace (a
+host runtime that only holds the tensors it was given, or a process whose
+device memory is reserved up front).  The no-allocation entry point takes the
+same parameters as kda_fwd_sm100 and draws its scratch from a fixed device
+array inside the library.  These tests call it through the C ABI and check it
+against the allocating entry point on two calls in a row (the array keeps the
+previous call's contents, so the second call checks that each call resets
+what it must), and that oversized problems are refused before any launch.
+
+This file is collected last on purpose: if it fails, a run that stops at the
+first failure has already run every other test.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from oracle.kda_oracle import max_rel
+from simpletrain_b200 import _ffi, device_status
+from simpletrain_b200.ops import _DTYPES, _decay_fields, _desc, _ptr, status_word
+from simpletrain_b200.workloads import custom, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL_LOWP = 2e-2    # bf16 outputs, normwise max|x-ref|/max|ref|
+TOL_STATE = 1e-3   # fp32 final state
+
+
+@pytest.fixture(autouse=True)
+def _needs_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _params(q, k, v, g, decay_bhd, s0, y, s_out, literal=False):
+    B, H, T, D = q.shape
+    dptr, dsb, dsh, dsd = _decay_fields(decay_bhd)
+    return _ffi.KdaFwdParams(
+        B, H, T, D, 64, _DTYPES[q.dtype], _ffi.KDA_FLAG_LITERAL if literal else 0,
+        _desc(q), _desc(k), _desc(v), _desc(g), _desc(y),
+        dptr, dsb, dsh, dsd, 0.0,
+        _ptr(s0), _ptr(s_out), None, 0, status_word(q.device).data_ptr())
+
+
+def _noalloc(q, k, v, g, decay_bhd, s0):
+    B, H, T, D = q.shape
+    y = torch.empty_like(q)
+    s_out = torch.empty(B, H, D, D, dtype=torch.float32, device=q.device)
+    p = _params(q, k, v, g, decay_bhd, s0, y, s_out)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = _ffi.load().kda_fwd_sm100_noalloc(ctypes.byref(p), stream)
+    assert rc == _ffi.KDA_OK, _ffi.status_string(rc)
+    return y, s_out
+
+
+@pytest.mark.parametrize("B,H,T,D", [(4, 6, 600, 128), (16, 10, 512, 128), (3, 5, 1000, 64)])
+def test_noalloc_matches_allocating_entry_point_twice(B, H, T, D):
+    w = custom(B, H, T, D, backward=False, s0_std=0.02)
+    inp = make_inputs(w, seed=3, device="cuda")
+    q, k, v, g, s0 = inp["q"], inp["k"], inp["v"], inp["g"], inp["s0"]
+    dec = inp["decay"].expand(B, H, D)
+    y_ref, s_ref = torch.ops.kda_b200.chunk_fwd(q, k, v, g, dec, 0.0, s0, 64, False, True)
+    for _ in range(2):
+        y, s = _noalloc(q, k, v, g, dec, s0)
+        torch.cuda.synchronize()
+        assert device_status() == 0
+        assert max_rel(y.float().cpu(), y_ref.float().cpu()) <= TOL_LOWP
+        assert max_rel(s.cpu(), s_ref.cpu()) <= TOL_STATE
+
+
+def test_noalloc_rejects_problems_larger_than_its_scratch():
+    lib = _ffi.load()
+    B, H, T, D = 1, 300, 64, 128          # 300 (batch, head) streams at D=128
+    assert lib.kda_fwd_workspace_bytes(B, H, T, D, 64, 0) > _ffi.NOALLOC_SCRATCH_BYTES
+    q = torch.zeros(B, H, T, D, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty_like(q)
+    dec = torch.full((B, H, D), 0.9, device="cuda")
+    p = _params(q, q, q, None, dec, None, y, None)
+    launches = _ffi.launch_count()
+    rc = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
+    assert rc == _ffi.KDA_ERR_WORKSPACE
+    assert _ffi.launch_count() == launches     # refused before anything was enqueued
