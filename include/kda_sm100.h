@@ -111,7 +111,11 @@ typedef struct kda_bwd_params {
   int32_t *status;
 } kda_bwd_params;
 
-/* Workspace needed by one call (0 allowed).  flags as in the params. */
+/* Workspace needed by one call on the CURRENT device (0 allowed).  flags as in
+   the params.  It holds one fp32 D x D state slot per boundary between the
+   call's work ranges (one range per resident CTA, so it is bounded by the
+   device's SM count, not by B*H or T), so query it on the device that runs
+   the call. */
 size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk,
                                uint32_t flags);
 size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk,
@@ -147,8 +151,10 @@ uint64_t kda_launch_count(void);
    the process exits.
    - Returns KDA_ERR_WORKSPACE, before enqueuing anything, when the problem
      needs more than KDA_NOALLOC_SCRATCH_BYTES of scratch
-     (kda_fwd_workspace_bytes() tells how much: 128 KiB per (batch, head) at
-     D=128, 32 KiB at D=64, plus a small header).
+     (kda_fwd_workspace_bytes() tells how much: 64 KiB per range boundary at
+     D=128, 16 KiB at D=64, at most one boundary per resident CTA -- about
+     10 MiB on a 148-SM GPU -- plus a small header; only a KDA_SM100_RANGES
+     override far above the CTA count reaches the limit).
    - The first call on a device looks up the array's device address; make that
      first call before any stream capture.
    - Calls share the array and it keeps the last call's contents; each call

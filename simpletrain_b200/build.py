@@ -51,15 +51,22 @@ def _hash() -> str:
     return h.hexdigest()
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
+TRACE_LIB = os.path.join(LIBDIR, "libkda_sm100_trace.so")
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    """Build the library; ``trace=True`` builds the development variant with
+    pipeline-event tracing into ``_lib/libkda_sm100_trace.so`` instead."""
     os.makedirs(LIBDIR, exist_ok=True)
+    lib, stamp = (TRACE_LIB, TRACE_LIB + ".srchash") if trace else (LIB, STAMP)
     digest = _hash()
-    if not force and os.path.exists(LIB) and os.path.exists(STAMP):
-        with open(STAMP) as fh:
+    if not force and os.path.exists(lib) and os.path.exists(stamp):
+        with open(stamp) as fh:
             if fh.read().strip() == digest:
-                return LIB
-    tmp = LIB + ".tmp"
-    cmd = [nvcc_path(), *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-o", tmp, *sources()]
+                return lib
+    tmp = lib + ".tmp"
+    extra = ["-DKDA_TRACE"] if trace else []
+    cmd = [nvcc_path(), *ARCH, *NVCC_FLAGS, *extra, "-I", os.path.join(ROOT, "include"), "-o", tmp, *sources()]
     if verbose:
         print(" ".join(cmd))
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -67,18 +74,19 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
     if verbose and (res.stdout or res.stderr):
         print(res.stdout + res.stderr)
-    os.replace(tmp, LIB)
-    with open(STAMP, "w") as fh:
+    os.replace(tmp, lib)
+    with open(stamp, "w") as fh:
         fh.write(digest)
-    return LIB
+    return lib
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="build the tracing development variant")
     args = ap.parse_args(argv)
-    print(build(force=args.force, verbose=args.verbose))
+    print(build(force=args.force, verbose=args.verbose, trace=args.trace))
 
 
 if __name__ == "__main__":

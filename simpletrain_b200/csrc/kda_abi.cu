@@ -68,64 +68,65 @@ int carry_f4(int D) { return (D == 128 ? 64 : 16) / 4; }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// workspace of one queue: [ticket][flags: nstreams ints][slots: nstreams x 2 x slot_f4 x 256 float4]
-size_t queue_header_bytes(int nstreams) { return align256(16 + 4 * (size_t)nstreams); }
-size_t queue_bytes(int nstreams, int slot_f4) {
-  return queue_header_bytes(nstreams) + (size_t)nstreams * 2 * slot_f4 * kda::tc::kEpi * 16;
-}
-
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 1;
 }
 
-// Segment length G (chunks per unit) minimising the modelled makespan
-// max(units per CTA slot, segments per chain) * (G + handoff), handoff = 1.5
-// chunks (state store + flag + reload, measured at the 1b shape).
-int choose_segment(int nstreams, int nchunks, int slots) {
-  int best_g = nchunks;
-  double best = 1e30;
-  for (int g = nchunks; g >= 1; --g) {
-    const int nseg = (nchunks + g - 1) / g;
-    if (nseg > 4096) break;
-    const long long units = (long long)nstreams * nseg;
-    const long long rounds = (units + slots - 1) / slots;
-    const double cost = (double)(rounds > nseg ? rounds : nseg) * (g + 1.5);
-    if (cost < best - 1e-9) {
-      best = cost;
-      best_g = g;
-    }
-  }
-  return best_g;
-}
-
-// Tuning override: KDA_SM100_SEGMENT=<chunks per unit> (0 or unset: automatic).
-int segment_override() {
+// Tuning override: KDA_SM100_RANGES=<ranges per launch> (0 or unset: one per CTA slot).
+int ranges_override() {
   static const int v = [] {
-    const char *s = std::getenv("KDA_SM100_SEGMENT");
+    const char *s = std::getenv("KDA_SM100_RANGES");
     return s ? std::atoi(s) : 0;
   }();
   return v;
 }
 
+// Ranges of one launch: one per resident CTA slot, at most one per chunk.
+int n_ranges(int nstreams, int nchunks, int slots) {
+  const long long n = (long long)nstreams * nchunks;
+  const int want = ranges_override() > 0 ? ranges_override() : slots;
+  return (int)(n < want ? n : want);
+}
+
+// CTA slots of each kernel on the current device (the launch and the workspace
+// query agree because both ask the same device).
+int fwd_slots(int D, bool literal) {
+  static std::atomic<int> cache[4];  // CTAs per SM by (D == 128, literal); 0 = not asked yet
+  std::atomic<int> &c = cache[(D == 128 ? 2 : 0) + (literal ? 1 : 0)];
+  int occ = c.load(std::memory_order_relaxed);
+  if (occ == 0) {
+    const int a = kda::fwd_tc_occupancy(D, KDA_DTYPE_BF16, literal);
+    const int b = kda::fwd_tc_occupancy(D, KDA_DTYPE_F16, literal);
+    occ = a > b ? a : b;
+    c.store(occ, std::memory_order_relaxed);
+  }
+  return sm_count() * occ;
+}
+int bwd_slots() { return sm_count(); }
+
+// workspace of one queue: [ticket][flags: nranges+1 ints][slots: (nranges+1) x slot_f4 x 256 float4]
+size_t queue_header_bytes(int nranges) { return align256(16 + 4 * ((size_t)nranges + 1)); }
+size_t queue_bytes(int nranges, int slot_f4) {
+  if (nranges <= 0) return 0;
+  return queue_header_bytes(nranges) + ((size_t)nranges + 1) * slot_f4 * kda::tc::kEpi * 16;
+}
+
 // Lay a queue over `ws` and clear its header on the stream.
-cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, int slot_f4, int slots, int *grid,
+cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, int slot_f4, int nranges,
                        cudaStream_t st) {
-  const int forced = segment_override();
-  const int g = forced > 0 ? (forced < nchunks ? forced : nchunks) : choose_segment(nstreams, nchunks, slots);
   q.ticket = reinterpret_cast<int *>(ws);
   q.flags = reinterpret_cast<int *>(reinterpret_cast<char *>(ws) + 16);
-  q.slots = reinterpret_cast<float4 *>(reinterpret_cast<char *>(ws) + queue_header_bytes(nstreams));
+  q.slots = reinterpret_cast<float4 *>(reinterpret_cast<char *>(ws) + queue_header_bytes(nranges));
   q.slot_f4 = slot_f4;
   q.nstreams = nstreams;
-  q.G = g;
   q.nchunks = nchunks;
-  q.nseg = (nchunks + g - 1) / g;
-  q.nunits = nstreams * q.nseg;
-  *grid = q.nunits < slots ? q.nunits : slots;
-  return cudaMemsetAsync(ws, 0, queue_header_bytes(nstreams), st);
+  q.nranges = nranges;
+  return cudaMemsetAsync(ws, 0, queue_header_bytes(nranges), st);
 }
+
+int n_chunks(int T, int chunk) { return chunk > 0 && T > 0 ? (T + chunk - 1) / chunk : 0; }
 
 }  // namespace
 
@@ -149,15 +150,17 @@ const char *kda_status_string(int32_t s) {
   }
 }
 
-size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t, int32_t D, int32_t, uint32_t) {
-  const int ns = (B > 0 ? B : 0) * (H > 0 ? H : 0);
-  return queue_bytes(ns, carry_f4(D));
+size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t flags) {
+  if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
+  const int nr = n_ranges(B * H, n_chunks(T, chunk), fwd_slots(D, (flags & KDA_FLAG_LITERAL) != 0));
+  return queue_bytes(nr, carry_f4(D));
 }
 
-size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t, int32_t D, int32_t, uint32_t) {
-  const int ns = (B > 0 ? B : 0) * (H > 0 ? H : 0);
+size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t) {
+  if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
+  const int nr = n_ranges(B * H, n_chunks(T, chunk), bwd_slots());
   // forward-direction pass: state, decay tangent, decay-gradient share; reverse pass: dS
-  return queue_bytes(ns, 2 * carry_f4(D) + 1) + queue_bytes(ns, carry_f4(D));
+  return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D));
 }
 
 int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
@@ -194,13 +197,12 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   a.s_in = p->state_in;
   a.s_out = p->state_out;
   a.status = p->status;
-  const int ns = p->B * p->H, nchunks = (p->T + p->chunk - 1) / p->chunk;
-  const int slots = sm_count() * kda::fwd_tc_occupancy(p->D, p->dtype, literal);
+  const int ns = p->B * p->H, nchunks = n_chunks(p->T, p->chunk);
+  const int nr = n_ranges(ns, nchunks, fwd_slots(p->D, literal));
   kda::tc::Queue q{};
-  int grid = 0;
-  cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), slots, &grid, st);
+  cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), nr, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(kda::launch_fwd_tc(a, q, grid, p->dtype, st));
+  return cuda_status(kda::launch_fwd_tc(a, q, nr, p->dtype, st));
 }
 
 int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
@@ -240,16 +242,15 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   a.ds_in = p->dstate_in;
   a.ddecay = p->ddecay;
   a.status = p->status;
-  const int ns = p->B * p->H, nchunks = (p->T + p->chunk - 1) / p->chunk;
-  const int slots = sm_count();
+  const int ns = p->B * p->H, nchunks = n_chunks(p->T, p->chunk);
+  const int nr = n_ranges(ns, nchunks, bwd_slots());
   const int f1 = 2 * carry_f4(p->D) + 1, f2 = carry_f4(p->D);
   kda::tc::Queue q1{}, q2{};
-  int g1 = 0, g2 = 0;
-  void *ws2 = reinterpret_cast<char *>(p->workspace) + queue_bytes(ns, f1);
-  cudaError_t e = make_queue(q1, p->workspace, ns, nchunks, f1, slots, &g1, st);
-  if (e == cudaSuccess) e = make_queue(q2, ws2, ns, nchunks, f2, slots, &g2, st);
+  void *ws2 = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, f1);
+  cudaError_t e = make_queue(q1, p->workspace, ns, nchunks, f1, nr, st);
+  if (e == cudaSuccess) e = make_queue(q2, ws2, ns, nchunks, f2, nr, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(kda::launch_bwd_tc(a, q1, q2, g1, g2, p->dtype, st));
+  return cuda_status(kda::launch_bwd_tc(a, q1, q2, nr, nr, p->dtype, st));
 }
 
 }  // extern "C"

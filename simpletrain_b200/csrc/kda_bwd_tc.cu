@@ -36,6 +36,7 @@ namespace kda {
 namespace {
 using namespace tc;
 
+
 template <int D, int NS>
 struct BwdLayout {
   static constexpr int KB = D / 64;
@@ -50,7 +51,7 @@ struct BwdLayout {
   static constexpr int BAR = SB + KB * PANEL;
   static constexpr int NBAR = 2 * NS + 20;
   static constexpr int RING = BAR + NBAR * 8;
-  static constexpr int RED = RING + 8;    // float [D] row sums
+  static constexpr int RED = RING + 16;   // float [D] row sums
   static constexpr int TMEM_SLOT = RED + 4 * D;
   static constexpr int ABORT = TMEM_SLOT + 8;
   static constexpr int SMEM = ABORT + 8 + 1024;
@@ -58,13 +59,13 @@ struct BwdLayout {
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
-// Unit-loop preamble shared by the MMA and epilogue roles.
+// Piece-loop preamble shared by the MMA and epilogue roles.
 #define KDA_TAKE_UNIT(REVERSE)                                                           \
   if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break; \
-  const int t = ring[i & 1];                                                             \
+  const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];                            \
   mbar_arrive(bar(UNIT_FREE0 + (i & 1)));                                                \
-  if (t >= qu.nunits) break;                                                             \
-  const Unit u = decode_unit(qu, t, REVERSE);
+  if (t >= qu.nranges) break;                                                            \
+  const Piece u = piece_of(qu, span_of(qu, t, REVERSE), p, REVERSE);
 
 // Producer: tickets and TMA loads of q, k, v, (g), dy for every chunk of every unit.
 template <int D, int NS>
@@ -81,32 +82,37 @@ __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, ui
   if (gate) prefetch_tmap(tg);
   prefetch_tmap(tdy);
   const uint32_t tx = (uint32_t)((4 + (gate ? 1 : 0)) * L::BOX);
-  int gc = 0;
-  for (int i = 0;; ++i) {
-    if (!mbar_wait(bar(UNIT_FREE0 + (i & 1)), ((i >> 1) & 1) ^ 1, a.status, abort_flag)) break;
+  int gc = 0, i = 0;
+  bool ok = true;
+  while (ok) {
     const int t = atomicAdd(qu.ticket, 1);
-    ring[i & 1] = t;
-    mbar_arrive(bar(UNIT_FULL0 + (i & 1)));
-    if (t >= qu.nunits) break;
-    const Unit u = decode_unit(qu, t, reverse);
-    const int b = u.stream / a.H, h = u.stream - b * a.H;
-    bool ok = true;
-    for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
-      const int c = reverse ? u.c_end - 1 - k : u.c_begin + k;
-      const int s = gc % NS, use = gc / NS;
-      if (!mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag)) { ok = false; break; }
-      const uint32_t st = sb + s * L::STAGE;
-      mbar_arrive_expect_tx(bar(FULL + s), tx);
-      for (int kb = 0; kb < L::KB; ++kb) {
-        const int x = 64 * kb, t0 = 64 * c;
-        tma_load_4d(st + L::ST_Q + kb * kTile, tq, bar(FULL + s), x, t0, h, b);
-        tma_load_4d(st + L::ST_K + kb * kTile, tk, bar(FULL + s), x, t0, h, b);
-        tma_load_4d(st + L::ST_V + kb * kTile, tv, bar(FULL + s), x, t0, h, b);
-        if (gate) tma_load_4d(st + L::ST_G + kb * kTile, tg, bar(FULL + s), x, t0, h, b);
-        tma_load_4d(st + L::ST_DY + kb * kTile, tdy, bar(FULL + s), x, t0, h, b);
+    const Span sp = t < qu.nranges ? span_of(qu, t, reverse) : Span{};
+    const int m = t < qu.nranges ? sp.npieces() : 1;
+    for (int p = 0; p < m && ok; ++p, ++i) {
+      if (!(ok = mbar_wait(bar(UNIT_FREE0 + (i & 1)), ((i >> 1) & 1) ^ 1, a.status, abort_flag))) break;
+      ring[2 * (i & 1)] = t;
+      ring[2 * (i & 1) + 1] = p;
+      mbar_arrive(bar(UNIT_FULL0 + (i & 1)));
+      if (t >= qu.nranges) { ok = false; break; }
+      const Piece u = piece_of(qu, sp, p, reverse);
+      const int b = u.stream / a.H, h = u.stream - b * a.H;
+      const int n = u.c_end - u.c_begin;
+      for (int k = 0; k < n; ++k, ++gc) {
+        const int c = reverse ? u.c_end - 1 - k : u.c_begin + k;
+        const int s = gc % NS, use = gc / NS;
+        if (!(ok = mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag))) break;
+        const uint32_t st = sb + s * L::STAGE;
+        mbar_arrive_expect_tx(bar(FULL + s), tx);
+        for (int kb = 0; kb < L::KB; ++kb) {
+          const int x = 64 * kb, t0 = 64 * c;
+          tma_load_4d(st + L::ST_Q + kb * kTile, tq, bar(FULL + s), x, t0, h, b);
+          tma_load_4d(st + L::ST_K + kb * kTile, tk, bar(FULL + s), x, t0, h, b);
+          tma_load_4d(st + L::ST_V + kb * kTile, tv, bar(FULL + s), x, t0, h, b);
+          if (gate) tma_load_4d(st + L::ST_G + kb * kTile, tg, bar(FULL + s), x, t0, h, b);
+          tma_load_4d(st + L::ST_DY + kb * kTile, tdy, bar(FULL + s), x, t0, h, b);
+        }
       }
     }
-    if (!ok) break;
   }
   for (int d = gc - 1; d >= 0 && d >= gc - NS; --d) mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
 }
@@ -274,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       KDA_TAKE_UNIT(false)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      if (!chain_wait(e, qu, u.stream, u.order, a.status, abort_flag)) break;
-      const float4 *prev = u.order > 0 ? slot_ptr(qu, u.stream, u.order - 1) : nullptr;
+      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      const float4 *prev = u.wait_slot >= 0 ? slot_ptr(qu, u.wait_slot) : nullptr;
       constexpr int CF4 = Carry<D>::FLOATS / 4;  // float4 per thread of one carry
       if (prev) {
         Td.load_slot(e, prev + CF4 * kEpi);
@@ -325,9 +331,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
                     u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
                   }
+                } else if (a.s_in) {
+                  const float4 *s4 = reinterpret_cast<const float4 *>(a.s_in + sbase + (size_t)row * D + col0);
+                  for (int q4 = 0; q4 < 8; ++q4) {
+                    const float4 v = __ldg(s4 + q4);
+                    u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
+                    u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
+                  }
                 } else {
-                  for (int k = 0; k < 32; ++k)
-                    u32[k] = __float_as_uint(a.s_in ? a.s_in[sbase + (size_t)row * D + col0 + k] : 0.f);
+                  for (int k = 0; k < 32; ++k) u32[k] = 0u;
                 }
               } else {
                 tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Z + col0, u32);
@@ -437,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // unit end: the last K^T V has landed in tensor memory
       if (!mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag)) break;
       tc_fence_after();
-      if (u.order + 1 < qu.nseg) {
-        float4 *slot = slot_ptr(qu, u.stream, u.order);
+      if (u.pub_slot >= 0) {
+        float4 *slot = slot_ptr(qu, u.pub_slot);
         {
           Carry<D> S;
           S.row[0] = Td.row[0];
@@ -449,13 +461,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         Td.store_slot(e, slot + CF4 * kEpi);
         __stcg(slot + 2 * CF4 * kEpi + e.et, make_float4(dl[0], dl[Carry<D>::NR - 1], 0.f, 0.f));
         tc_fence_before();
-        chain_publish(e, qu, u.stream, u.order);
+        chain_publish(e, qu, u.pub_slot);
       } else if (want_dd) {
         // <dS_T, T_T> row-wise, then the two column halves of every row meet in smem
-        for (int r = 0; r < Carry<D>::NR; ++r) {
-          if (a.ds_out)
-            for (int k = 0; k < Carry<D>::NV; ++k)
-              dl[r] = fmaf(a.ds_out[sbase + (size_t)Td.row[r] * D + Td.col(e, k)], Td.x[r][k], dl[r]);
+        if (a.ds_out) {
+          Carry<D> dST;
+          dST.row[0] = Td.row[0];
+          dST.row[Carry<D>::NR - 1] = Td.row[Carry<D>::NR - 1];
+          dST.load_rm(e, a.ds_out + sbase);
+          for (int r = 0; r < Carry<D>::NR; ++r)
+            for (int k = 0; k < Carry<D>::NV; ++k) dl[r] = fmaf(dST.x[r][k], Td.x[r][k], dl[r]);
         }
         named_bar_sync(1, kEpi);
         if (e.et < D) red[e.et] = 0.f;
@@ -627,9 +642,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       KDA_TAKE_UNIT(true)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      if (!chain_wait(e, qu, u.stream, u.order, a.status, abort_flag)) break;
-      if (u.order == 0) dS.load_rm(e, a.ds_out ? a.ds_out + sbase : nullptr);
-      else dS.load_slot(e, slot_ptr(qu, u.stream, u.order - 1));
+      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      if (u.wait_slot < 0) dS.load_rm(e, a.ds_out ? a.ds_out + sbase : nullptr);
+      else dS.load_slot(e, slot_ptr(qu, u.wait_slot));
       float af[Carry<D>::NR], at[Carry<D>::NR];
       const int Ltail = a.T - (qu.nchunks - 1) * 64;
       for (int r = 0; r < Carry<D>::NR; ++r) {
@@ -721,9 +736,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      if (u.order + 1 < qu.nseg) {
-        dS.store_slot(e, slot_ptr(qu, u.stream, u.order));
-        chain_publish(e, qu, u.stream, u.order);
+      if (u.pub_slot >= 0) {
+        dS.store_slot(e, slot_ptr(qu, u.pub_slot));
+        chain_publish(e, qu, u.pub_slot);
       } else if (a.ds_in) {
         dS.store_rm(e, a.ds_in + sbase);
       }

@@ -17,6 +17,11 @@
 // unit tickets; warp 1 owns tensor memory and one thread issues the MMAs;
 // warps 2-9 run the epilogue (two per TMEM sub-partition).  A unit starts
 // from its chain predecessor's published state and publishes its own.
+//
+// Pipelining: O is double-buffered in tensor memory and the epilogue runs
+// "state update of c -> store y_c -> mask P_{c+1}", so the MMAs of chunk c+1
+// (Q K^T, Q S_c, K^T V) execute while y_c is gated and stored.  y leaves
+// through a double-buffered smem tile and TMA stores.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -27,6 +32,8 @@
 #include "kda_tc_epi.cuh"
 #include "tmap.h"
 
+KDA_TRACE_DEFINE
+
 namespace kda {
 namespace {
 using namespace tc;
@@ -35,24 +42,25 @@ template <int D, int NS>
 struct FwdLayout {
   static constexpr int KB = D / 64;
   static constexpr int BOX = KB * kTile;
-  static constexpr int ST_Q = 0, ST_K = BOX, ST_V = 2 * BOX, ST_G = 3 * BOX, STAGE = 4 * BOX;
+  static constexpr int ST_Q = 0, ST_K = BOX, ST_V = 2 * BOX, STAGE = 3 * BOX;  // g is read from global
   static constexpr int P = NS * STAGE;
   static constexpr int SB = P + kTile;  // S_{c-1}: KB panels of [D rows x 64]
-  static constexpr int BAR = SB + KB * D * 128;
-  static constexpr int NBAR = 2 * NS + 15;
-  static constexpr int RING = BAR + NBAR * 8;  // two unit tickets
-  static constexpr int TMEM_SLOT = RING + 8;
+  static constexpr int Y = SB + KB * D * 128;  // two y staging tiles (BOX each)
+  static constexpr int BAR = Y + 2 * BOX;
+  static constexpr int NBAR = 2 * NS + 16;
+  static constexpr int RING = BAR + NBAR * 8;  // two (ticket, piece) entries
+  static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
   static constexpr int SMEM = ABORT + 8 + 1024;
-  static constexpr uint32_t A_QK = 0, A_O = 64, A_KV = 64 + D;
-  static constexpr uint32_t TMEM_COLS = (64 + 2 * D) <= 256 ? 256 : 512;
+  static constexpr uint32_t A_QK = 0, A_O0 = 64, A_O1 = 64 + D, A_KV = 64 + 2 * D;
+  static constexpr uint32_t TMEM_COLS = (64 + 3 * D) <= 256 ? 256 : 512;
 };
 
 template <typename T, int D, bool LIT, int NS>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg, const FwdArgs a,
-                  const Queue qu) {
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
+                  const __grid_constant__ CUtensorMap ty, const FwdArgs a, const Queue qu) {
   using L = FwdLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr int KB = L::KB;
@@ -61,8 +69,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
   enum {
-    QK_FULL = 2 * NS, QK_FREE, S_READY, O_FREE, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0, UNIT_FULL1,
-    UNIT_FREE0, UNIT_FREE1, FIN
+    QK_FULL = 2 * NS, QK_FREE, S_READY, O_FREE0, O_FREE1, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0,
+    UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -71,23 +79,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool gate = a.g.data != nullptr;
 
   if (threadIdx.x == 0) {
+    KDA_TRACE_CTA(0, kda_globaltimer());
+    KDA_TRACE_CTA(7, kda_smid());
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar(FULL + s), 1);
-      mbar_init(bar(EMPTY + s), 2);  // MMA commit + epilogue (done with the gate tile)
+      mbar_init(bar(EMPTY + s), 1);  // MMA commit
     }
     mbar_init(bar(QK_FULL + 0), 1);
     mbar_init(bar(QK_FULL + 1), kEpi);
     mbar_init(bar(QK_FULL + 2), 1);
     mbar_init(bar(QK_FULL + 3), kEpi);
     mbar_init(bar(QK_FULL + 4), kEpi);
-    mbar_init(bar(QK_FULL + 5), 1);
+    mbar_init(bar(QK_FULL + 5), kEpi);
     mbar_init(bar(QK_FULL + 6), 1);
     mbar_init(bar(QK_FULL + 7), 1);
     mbar_init(bar(QK_FULL + 8), 1);
     mbar_init(bar(QK_FULL + 9), 1);
-    mbar_init(bar(QK_FULL + 10), 1 + kEpi);
+    mbar_init(bar(QK_FULL + 10), 1);
     mbar_init(bar(QK_FULL + 11), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 12), 1);
+    mbar_init(bar(QK_FULL + 12), 1 + kEpi);
+    mbar_init(bar(QK_FULL + 13), 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -105,31 +116,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
-      if (gate) prefetch_tmap(&tg);
-      const uint32_t tx = (uint32_t)((3 + (gate ? 1 : 0)) * L::BOX);
-      int gc = 0;
-      for (int i = 0;; ++i) {
-        if (!mbar_wait(bar(UNIT_FREE0 + (i & 1)), ((i >> 1) & 1) ^ 1, a.status, abort_flag)) break;
+      prefetch_tmap(&ty);
+      const uint32_t tx = (uint32_t)(3 * L::BOX);
+      int gc = 0, i = 0;
+      bool ok = true;
+      while (ok) {
         const int t = atomicAdd(qu.ticket, 1);
-        ring[i & 1] = t;
-        mbar_arrive(bar(UNIT_FULL0 + (i & 1)));
-        if (t >= qu.nunits) break;
-        const Unit u = decode_unit(qu, t, false);
-        const int b = u.stream / a.H, h = u.stream - b * a.H;
-        bool ok = true;
-        for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
-          const int s = gc % NS, use = gc / NS;
-          if (!mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag)) { ok = false; break; }
-          const uint32_t st = sb + s * L::STAGE;
-          mbar_arrive_expect_tx(bar(FULL + s), tx);
-          for (int kb = 0; kb < KB; ++kb) {
-            tma_load_4d(st + L::ST_Q + kb * kTile, &tq, bar(FULL + s), 64 * kb, 64 * c, h, b);
-            tma_load_4d(st + L::ST_K + kb * kTile, &tk, bar(FULL + s), 64 * kb, 64 * c, h, b);
-            tma_load_4d(st + L::ST_V + kb * kTile, &tv, bar(FULL + s), 64 * kb, 64 * c, h, b);
-            if (gate) tma_load_4d(st + L::ST_G + kb * kTile, &tg, bar(FULL + s), 64 * kb, 64 * c, h, b);
+        const Span sp = t < qu.nranges ? span_of(qu, t, false) : Span{};
+        const int m = t < qu.nranges ? sp.npieces() : 1;
+        for (int p = 0; p < m && ok; ++p, ++i) {
+          if (!(ok = mbar_wait(bar(UNIT_FREE0 + (i & 1)), ((i >> 1) & 1) ^ 1, a.status, abort_flag))) break;
+          ring[2 * (i & 1)] = t;
+          ring[2 * (i & 1) + 1] = p;
+          mbar_arrive(bar(UNIT_FULL0 + (i & 1)));
+          if (t >= qu.nranges) { ok = false; break; }
+          const Piece u = piece_of(qu, sp, p, false);
+          const int b = u.stream / a.H, h = u.stream - b * a.H;
+          for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
+            const int s = gc % NS, use = gc / NS;
+            if (!(ok = mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag))) break;
+            KDA_TRACE_EVENT(0, gc);
+            const uint32_t st = sb + s * L::STAGE;
+            mbar_arrive_expect_tx(bar(FULL + s), tx);
+            for (int kb = 0; kb < KB; ++kb) {
+              tma_load_4d(st + L::ST_Q + kb * kTile, &tq, bar(FULL + s), 64 * kb, 64 * c, h, b);
+              tma_load_4d(st + L::ST_K + kb * kTile, &tk, bar(FULL + s), 64 * kb, 64 * c, h, b);
+              tma_load_4d(st + L::ST_V + kb * kTile, &tv, bar(FULL + s), 64 * kb, 64 * c, h, b);
+            }
+            KDA_TRACE_EVENT(1, gc);
           }
         }
-        if (!ok) break;
       }
       for (int d = gc - 1; d >= 0 && d >= gc - NS; --d)
         mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
@@ -145,16 +161,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int gc = 0;
       for (int i = 0;; ++i) {
         if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break;
-        const int t = ring[i & 1];
+        const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
         mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
-        if (t >= qu.nunits) break;
-        const Unit u = decode_unit(qu, t, false);
+        if (t >= qu.nranges) break;
+        const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
         bool ok = true;
         for (int c = u.c_begin; c < u.c_end && ok; ++c, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
-          ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
-               mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag);
+          ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag);
+          KDA_TRACE_EVENT(2, gc);
+          ok = ok && mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag);
           if (!ok) break;
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
@@ -162,16 +179,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16(tmem + L::A_QK, sdesc_k(st + L::ST_Q + off), sdesc_k(st + L::ST_K + off), id_qk, ks > 0);
           }
           mma_commit(bar(QK_FULL));
-          ok = mbar_wait(bar(S_READY), ph, a.status, abort_flag) &&
-               mbar_wait(bar(O_FREE), ph ^ 1, a.status, abort_flag);
+          const int ob = gc & 1;
+          const uint32_t acc_o = ob ? L::A_O1 : L::A_O0;
+          ok = mbar_wait(bar(S_READY), ph, a.status, abort_flag);
+          KDA_TRACE_EVENT(3, gc);
+          ok = ok && mbar_wait(bar(O_FREE0 + ob), ((gc >> 1) & 1) ^ 1, a.status, abort_flag);
+          KDA_TRACE_EVENT(4, gc);
           if (!ok) break;
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
-            mma_f16(tmem + L::A_O, sdesc_k(st + L::ST_Q + off), sdesc_mn(sb + L::SB + ks * 2048, D * 128), id_qs,
+            mma_f16(tmem + acc_o, sdesc_k(st + L::ST_Q + off), sdesc_mn(sb + L::SB + ks * 2048, D * 128), id_qs,
                     ks > 0);
           }
           if (!(ok = mbar_wait(bar(KV_FREE), ph ^ 1, a.status, abort_flag))) break;
+          KDA_TRACE_EVENT(5, gc);
           tc_fence_after();
           for (int ks = 0; ks < 4; ++ks) {
             if (LIT)
@@ -183,9 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mma_commit(bar(KV_FULL));
           if (!(ok = mbar_wait(bar(P_FULL), ph, a.status, abort_flag))) break;
+          KDA_TRACE_EVENT(6, gc);
           tc_fence_after();
           for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + L::A_O, sdesc_k(sb + L::P + ks * 32), sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_pv,
+            mma_f16(tmem + acc_o, sdesc_k(sb + L::P + ks * 32), sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_pv,
                     1);
           mma_commit(bar(O_FULL));
           mma_commit(bar(EMPTY + s));
@@ -204,16 +227,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gc = 0;
     for (int i = 0;; ++i) {
       if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break;
-      const int t = ring[i & 1];
+      const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
       mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
-      if (t >= qu.nunits) break;
-      const Unit u = decode_unit(qu, t, false);
+      if (t >= qu.nranges) break;
+      const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      // unit-start state: initial state or the chain predecessor's
-      if (!chain_wait(e, qu, u.stream, u.order, a.status, abort_flag)) break;
-      if (u.order == 0) S.load_rm(e, a.s_in ? a.s_in + sbase : nullptr);
-      else S.load_slot(e, slot_ptr(qu, u.stream, u.order - 1));
+      // piece-start state: the initial state, or the one published at the range boundary
+      if (e.et == 0) KDA_TRACE_EVENT(15, gc);
+      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      if (e.et == 0) KDA_TRACE_EVENT(16, gc);
+      if (u.wait_slot < 0) S.load_rm(e, a.s_in ? a.s_in + sbase : nullptr);
+      else S.load_slot(e, slot_ptr(qu, u.wait_slot));
       float af[Carry<D>::NR], at[Carry<D>::NR];
       const int Ltail = a.T - (qu.nchunks - 1) * 64;
       for (int r = 0; r < Carry<D>::NR; ++r) {
@@ -223,22 +248,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       S.template write_operand<BF>(e, sb + L::SB);
       fence_async_smem();
       named_bar_sync(1, kEpi);
-      if (e.et == 0) mbar_arrive(bar(S_READY));
-      bool ok = true;
-      for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
-        const int s = gc % NS, use = gc / NS, ph = gc & 1;
-        const uint32_t st = sb + s * L::STAGE;
-        const int t0 = 64 * c, Lc = min(64, a.T - t0);
-        // (a) masked scores -> P
-        if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
+      if (e.et == 0) {
+        mbar_arrive(bar(S_READY));
+        if (i == 0) KDA_TRACE_CTA(1, kda_globaltimer());
+      }
+      // masked scores -> P for chunk gc (its Q K^T was issued ahead)
+      auto make_p = [&](int g) -> bool {
+        if (e.et == 0) KDA_TRACE_EVENT(12, g);
+        if (!mbar_wait(bar(QK_FULL), g & 1, a.status, abort_flag)) return false;
+        if (e.et == 0) KDA_TRACE_EVENT(13, g);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
         mbar_arrive(bar(QK_FREE));
         fence_async_smem();
         named_bar_sync(1, kEpi);
-        if (e.et == 0) mbar_arrive(bar(P_FULL));
+        if (e.et == 0) {
+          mbar_arrive(bar(P_FULL));
+          KDA_TRACE_EVENT(14, g);
+        }
+        return true;
+      };
+      bool ok = make_p(gc);
+      for (int c = u.c_begin; c < u.c_end && ok; ++c, ++gc) {
+        const int ph = gc & 1, ob = gc & 1;
+        const int t0 = 64 * c, Lc = min(64, a.T - t0);
+        const bool last = c + 1 == u.c_end;
+        // gate fragment for y_c straight from global memory; lands during the state update
+        uint32_t gfr[D / 8];
+        if (gate) {
+          const uint16_t *gp = reinterpret_cast<const uint16_t *>(a.g.data) + b * a.g.sb + h * a.g.sh;
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee) {
+              const int row = e.r0 + 8 * ee;
+              gfr[2 * j + ee] = row < Lc ? __ldg(reinterpret_cast<const unsigned int *>(
+                                               gp + (int64_t)(t0 + row) * a.g.st + (D / 2) * e.half + 8 * j + e.cq))
+                                         : 0u;
+            }
+        }
         // (b) S_c = decay^L S_{c-1} + U_c  (U_c's MMA follows Q S_{c-1}, so the operand is free)
         if (!(ok = mbar_wait(bar(KV_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(8, gc);
         tc_fence_after();
         {
           const bool upd = !(LIT && Lc != 64);
@@ -262,49 +311,64 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(bar(KV_FREE));
         }
-        if (c + 1 < u.c_end) {
+        if (!last) {
           S.template write_operand<BF>(e, sb + L::SB);
           fence_async_smem();
           named_bar_sync(1, kEpi);
-          if (e.et == 0) mbar_arrive(bar(S_READY));
+          if (e.et == 0) {
+            mbar_arrive(bar(S_READY));
+            KDA_TRACE_EVENT(9, gc);
+          }
+        } else if (u.pub_slot >= 0) {
+          // hand the state across the range boundary before storing the last y
+          S.store_slot(e, slot_ptr(qu, u.pub_slot));
+          chain_publish(e, qu, u.pub_slot);
+        } else if (a.s_out) {
+          S.store_rm(e, a.s_out + sbase);
         }
-        // (c) y_c = g_c * O_c
-        if (!(ok = mbar_wait(bar(O_FULL), ph, a.status, abort_flag) &&
-                   mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag)))
-          break;
+        // (c) y_c = g_c * O_c  -> staging tile -> TMA store
+        if (e.et == 0) KDA_TRACE_EVENT(7, gc);
+        if (!(ok = mbar_wait(bar(O_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(10, gc);
         tc_fence_after();
         {
           Frag<D / 2> fo;
-          ld_frag(tmem + e.lane_off + L::A_O + (D / 2) * e.half, fo);
+          ld_frag(tmem + e.lane_off + (ob ? L::A_O1 : L::A_O0) + (D / 2) * e.half, fo);
           tc_fence_before();
-          mbar_arrive(bar(O_FREE));
-          float y[D / 2];
+          mbar_arrive(bar(O_FREE0 + ob));
+          const uint32_t yt = sb + L::Y + ob * L::BOX;
+          if (e.et == 0) tma_store_wait_read1();  // the store that used this tile two chunks ago has read it
+          named_bar_sync(1, kEpi);
           for (int j = 0; j < D / 16; ++j) {
             const int col = (D / 2) * e.half + 8 * j + e.cq;
             for (int ee = 0; ee < 2; ++ee) {
+              const int row = e.r0 + 8 * ee;
               float o0 = fo.v(ee, j, 0), o1 = fo.v(ee, j, 1);
               if (gate) {
-                const float2 g2 = unpack2(ld_shared_u32(box_addr(st + L::ST_G, e.r0 + 8 * ee, col)), BF);
+                const float2 g2 = unpack2(gfr[2 * j + ee], BF);
                 o0 *= g2.x;
                 o1 *= g2.y;
               }
-              y[4 * j + 2 * ee] = o0;
-              y[4 * j + 2 * ee + 1] = o1;
+              st_shared_u32(box_addr(yt, row, col), pack2(o0, o1, BF));
             }
           }
+          fence_async_smem();
           named_bar_sync(1, kEpi);
-          if (e.et == 0) mbar_arrive(bar(EMPTY + s));  // gate tile read
-          store_frag_global<D, BF>(e, y, a.y, b, h, t0, Lc);
+          if (e.et == 0) {
+            for (int kb = 0; kb < KB; ++kb) tma_store_4d(&ty, yt + kb * kTile, 64 * kb, t0, h, b);
+            tma_store_commit();
+            KDA_TRACE_EVENT(11, gc);
+          }
         }
+        // (a) P for the next chunk of the unit
+        if (!last) ok = make_p(gc + 1);
       }
       if (!ok) break;
-      // unit end: hand the state to the next segment, or return it
-      if (u.order + 1 < qu.nseg) {
-        S.store_slot(e, slot_ptr(qu, u.stream, u.order));
-        chain_publish(e, qu, u.stream, u.order);
-      } else if (a.s_out) {
-        S.store_rm(e, a.s_out + sbase);
-      }
+    }
+    if (e.et == 0) {
+      tma_store_wait_all();
+      KDA_TRACE_CTA(2, kda_globaltimer());
+      KDA_TRACE_CTA(3, gc);
     }
   }
   __syncthreads();
@@ -317,16 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T, int D, bool LIT, int NS>
 cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap mq, mk, mv, mg;
+  CUtensorMap mq, mk, mv, mg, my;
   const View gview = a.g.data ? a.g : a.q;
   if (!make_tmap_bhtd(&mq, a.q, a.B, a.H, a.T, a.D, BF) || !make_tmap_bhtd(&mk, a.k, a.B, a.H, a.T, a.D, BF) ||
-      !make_tmap_bhtd(&mv, a.v, a.B, a.H, a.T, a.D, BF) || !make_tmap_bhtd(&mg, gview, a.B, a.H, a.T, a.D, BF))
+      !make_tmap_bhtd(&mv, a.v, a.B, a.H, a.T, a.D, BF) || !make_tmap_bhtd(&mg, gview, a.B, a.H, a.T, a.D, BF) ||
+      !make_tmap_bhtd(&my, a.y, a.B, a.H, a.T, a.D, BF))
     return cudaErrorInvalidValue;
   using L = FwdLayout<D, NS>;
   auto kern = fwd_tc_kernel<T, D, LIT, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, a, q);
+  kern<<<grid, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -345,20 +410,29 @@ int fwd_ctas_per_sm() {
 int fwd_tc_occupancy(int D, int dtype, bool literal) {
   const bool bf = dtype == KDA_DTYPE_BF16;
   if (D == 64) {
-    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true, 2>() : fwd_ctas_per_sm<__half, 64, true, 2>();
-    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, 2>() : fwd_ctas_per_sm<__half, 64, false, 2>();
+    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true, 3>() : fwd_ctas_per_sm<__half, 64, true, 3>();
+    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, 3>() : fwd_ctas_per_sm<__half, 64, false, 3>();
   }
-  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, 2>() : fwd_ctas_per_sm<__half, 128, false, 2>();
+  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, 3>() : fwd_ctas_per_sm<__half, 128, false, 3>();
 }
 
 cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dtype, cudaStream_t st) {
   const bool bf = dtype == KDA_DTYPE_BF16;
   if (a.D == 64) {
     if (a.literal)
-      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true, 2>(a, q, grid, st) : fwd_tc_launch<__half, 64, true, 2>(a, q, grid, st);
-    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, 2>(a, q, grid, st) : fwd_tc_launch<__half, 64, false, 2>(a, q, grid, st);
+      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true, 3>(a, q, grid, st) : fwd_tc_launch<__half, 64, true, 3>(a, q, grid, st);
+    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, 3>(a, q, grid, st) : fwd_tc_launch<__half, 64, false, 3>(a, q, grid, st);
   }
-  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, 2>(a, q, grid, st) : fwd_tc_launch<__half, 128, false, 2>(a, q, grid, st);
+  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, 3>(a, q, grid, st) : fwd_tc_launch<__half, 128, false, 3>(a, q, grid, st);
 }
 
 }  // namespace kda
+
+#ifdef KDA_TRACE
+extern "C" int kda_trace_copy_fwd(unsigned long long *host) {
+  return (int)cudaMemcpyFromSymbol(host, g_kda_trace, sizeof(g_kda_trace));
+}
+extern "C" int kda_trace_copy_fwd_cta(unsigned long long *host) {
+  return (int)cudaMemcpyFromSymbol(host, g_kda_trace_cta, sizeof(g_kda_trace_cta));
+}
+#endif

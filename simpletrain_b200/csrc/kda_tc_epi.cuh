@@ -2,14 +2,21 @@
 // memory fragments, the fp32 carry (state) layout, smem tile helpers, direct
 // global stores, and the persistent work queue with chained state handoff.
 //
-// Scheduling.  The scan over T is cut into segments of G chunks.  A "stream"
-// is one (batch, head); a unit is (stream, segment).  Persistent CTAs take
-// unit tickets from an atomic counter in the workspace; tickets are issued
-// segment-major in chain order, so a unit only ever waits for a unit with a
-// smaller ticket, which some running CTA holds (no deadlock).  A unit starts
-// from the state its chain predecessor published (or from the initial state),
-// and publishes its own end state into a two-slot ring per stream.  Every
-// wait is bounded.
+// Scheduling.  A "stream" is one (batch, head).  The stream-major sequence of
+// all (stream, chunk) pairs is cut into `nranges` contiguous ranges of equal
+// length (to one chunk), one per persistent CTA slot; CTAs take range tickets
+// from an atomic counter in the workspace.  A range is split at stream
+// boundaries into pieces: at most a partial first piece (the end of a stream
+// begun by the range before), whole streams, and at most a partial last piece
+// (the start of a stream finished by the range after).  The carried state
+// crosses a range boundary through one slot per boundary.  Pieces run in an
+// order that makes the boundary wait cheap: in the forward direction the last
+// piece (a stream start, no wait) runs first and publishes its end state, the
+// first piece (which waits for the previous range's publish) runs last; the
+// reverse direction mirrors this with the ranges ticketed last-to-first.  A
+// range therefore only waits for a range ticketed before it, which a running
+// CTA holds (no deadlock), and usually for a piece finished long before.
+// Every wait is bounded.
 #pragma once
 
 #include <cuda.h>
@@ -17,6 +24,42 @@
 
 #include "kda_internal.h"
 #include "tc_common.cuh"
+
+// Development tracing: built only with -DKDA_TRACE (python -m simpletrain_b200.build
+// --trace writes a separate library); records clock64() of pipeline events of
+// CTA 0 into a per-kernel-file device array [chunk][32 slots], and the global
+// timer (ns) of per-CTA milestones into [CTA][8 slots] (slot 7: SM id).
+#ifdef KDA_TRACE
+#define KDA_TRACE_DEFINE                                      \
+  static __device__ unsigned long long g_kda_trace[128 * 32]; \
+  static __device__ unsigned long long g_kda_trace_cta[1024 * 8];
+#define KDA_TRACE_EVENT(slot, chunk)                                                    \
+  do {                                                                                  \
+    if (blockIdx.x == 0 && (chunk) < 128) g_kda_trace[(chunk) * 32 + (slot)] = clock64(); \
+  } while (0)
+#define KDA_TRACE_CTA(slot, value)                                              \
+  do {                                                                          \
+    if (blockIdx.x < 1024) g_kda_trace_cta[blockIdx.x * 8 + (slot)] = (value); \
+  } while (0)
+__device__ __forceinline__ unsigned long long kda_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned kda_smid() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %smid;" : "=r"(r));
+  return r;
+}
+#else
+#define KDA_TRACE_DEFINE
+#define KDA_TRACE_EVENT(slot, chunk) \
+  do {                               \
+  } while (0)
+#define KDA_TRACE_CTA(slot, value) \
+  do {                             \
+  } while (0)
+#endif
 
 namespace kda {
 namespace tc {
@@ -83,14 +126,37 @@ struct Carry {
     for (int r = 0; r < NR; ++r)
       for (int i = 0; i < NV; ++i) x[r][i] = 0.f;
   }
-  // row-major [D][D] fp32 (user-facing states)
+  // row-major [D][D] fp32 (user-facing states, 16-byte aligned), in the widest
+  // accesses the layout allows: float4 runs of a row (D=128), float2 pairs (D=64)
   __device__ void load_rm(const Epi &e, const float *src) {
-    for (int r = 0; r < NR; ++r)
-      for (int i = 0; i < NV; ++i) x[r][i] = src ? src[(size_t)row[r] * D + col(e, i)] : 0.f;
+    if (src == nullptr) {
+      zero();
+      return;
+    }
+    if (D == 128) {
+      const float4 *s4 = reinterpret_cast<const float4 *>(src + (size_t)row[0] * D + 64 * e.half);
+      for (int i = 0; i < 16; ++i) {
+        const float4 v = __ldg(s4 + i);
+        x[0][4 * i] = v.x; x[0][4 * i + 1] = v.y; x[0][4 * i + 2] = v.z; x[0][4 * i + 3] = v.w;
+      }
+    } else {
+      for (int r = 0; r < NR; ++r)
+        for (int j = 0; j < NV / 2; ++j) {
+          const float2 v = __ldg(reinterpret_cast<const float2 *>(src + (size_t)row[r] * D + col(e, 2 * j)));
+          x[r][2 * j] = v.x;
+          x[r][2 * j + 1] = v.y;
+        }
+    }
   }
   __device__ void store_rm(const Epi &e, float *dst) const {
-    for (int r = 0; r < NR; ++r)
-      for (int i = 0; i < NV; ++i) dst[(size_t)row[r] * D + col(e, i)] = x[r][i];
+    if (D == 128) {
+      float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)row[0] * D + 64 * e.half);
+      for (int i = 0; i < 16; ++i) d4[i] = make_float4(x[0][4 * i], x[0][4 * i + 1], x[0][4 * i + 2], x[0][4 * i + 3]);
+    } else {
+      for (int r = 0; r < NR; ++r)
+        for (int j = 0; j < NV / 2; ++j)
+          *reinterpret_cast<float2 *>(dst + (size_t)row[r] * D + col(e, 2 * j)) = make_float2(x[r][2 * j], x[r][2 * j + 1]);
+    }
   }
   // handoff slot layout: float4 index i4 of thread et at slot[i4 * kEpi + et]
   __device__ void store_slot(const Epi &e, float4 *slot) const {
@@ -240,28 +306,55 @@ __device__ void store_frag_global(const Epi &e, const float (&val)[D / 2], const
 // ------------------------------------------------------------ scheduling --
 struct Queue {
   int *ticket;     // tickets taken so far (cleared by the host before the launch)
-  int *flags;      // [nstreams]: chain positions published per stream (cleared by the host)
-  float4 *slots;   // [nstreams][2][slot_f4 * kEpi]
+  int *flags;      // [nranges + 1]: boundary slot published (cleared by the host)
+  float4 *slots;   // [nranges + 1][slot_f4 * kEpi]: carried state at range boundary r
   int slot_f4;     // float4 per thread per slot
-  int nstreams, nseg, G, nchunks, nunits;
+  int nstreams, nchunks, nranges;
 };
 
-struct Unit {
-  int stream, seg, order, c_begin, c_end;  // chunks [c_begin, c_end)
+struct Piece {
+  int stream, c_begin, c_end;  // chunks [c_begin, c_end) of one stream
+  int wait_slot;               // boundary slot holding the entry state, or -1 (stream end / start)
+  int pub_slot;                // boundary slot for the exit state, or -1
 };
 
-__device__ __forceinline__ Unit decode_unit(const Queue &qu, int t, bool reverse) {
-  Unit u;
-  u.order = t / qu.nstreams;
-  u.stream = t - u.order * qu.nstreams;
-  u.seg = reverse ? qu.nseg - 1 - u.order : u.order;
-  u.c_begin = u.seg * qu.G;
-  u.c_end = min(qu.nchunks, u.c_begin + qu.G);
-  return u;
+// Range of ticket t: stream-major positions [N t / R, N (t+1) / R), N = streams x chunks.
+struct Span {
+  int r, s0, c0, s1, c1;  // first piece (s0, [c0, ...)), last piece (s1, [..., c1))
+  __device__ __forceinline__ int npieces() const { return s1 - s0 + 1; }
+};
+
+__device__ __forceinline__ Span span_of(const Queue &qu, int t, bool reverse) {
+  Span sp;
+  sp.r = reverse ? qu.nranges - 1 - t : t;
+  const long long n = (long long)qu.nstreams * qu.nchunks;
+  const long long lo = n * sp.r / qu.nranges, hi = n * (sp.r + 1) / qu.nranges;
+  sp.s0 = (int)(lo / qu.nchunks);
+  sp.c0 = (int)(lo - (long long)sp.s0 * qu.nchunks);
+  sp.s1 = (int)((hi - 1) / qu.nchunks);
+  sp.c1 = (int)(hi - (long long)sp.s1 * qu.nchunks);
+  return sp;
 }
 
-__device__ __forceinline__ float4 *slot_ptr(const Queue &qu, int stream, int order) {
-  return qu.slots + ((size_t)stream * 2 + (order & 1)) * (size_t)qu.slot_f4 * kEpi;
+// Piece p (in processing order) of a span.  Forward: last piece, the whole
+// streams, first piece.  Reverse: first piece, whole streams, last piece.
+__device__ __forceinline__ Piece piece_of(const Queue &qu, const Span &sp, int p, bool reverse) {
+  const int m = sp.npieces();
+  int s;
+  if (reverse || m == 1) s = sp.s0 + p;
+  else s = p == 0 ? sp.s1 : (p == m - 1 ? sp.s0 : sp.s0 + p);
+  Piece pc;
+  pc.stream = s;
+  pc.c_begin = s == sp.s0 ? sp.c0 : 0;
+  pc.c_end = s == sp.s1 ? sp.c1 : qu.nchunks;
+  const int at_begin = pc.c_begin > 0 ? sp.r : -1, at_end = pc.c_end < qu.nchunks ? sp.r + 1 : -1;
+  pc.wait_slot = reverse ? at_end : at_begin;
+  pc.pub_slot = reverse ? at_begin : at_end;
+  return pc;
+}
+
+__device__ __forceinline__ float4 *slot_ptr(const Queue &qu, int slot) {
+  return qu.slots + (size_t)slot * qu.slot_f4 * kEpi;
 }
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
@@ -270,16 +363,16 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   return v;
 }
 
-// Epilogue: wait until the chain predecessor of `order` has published (one
-// thread spins, bounded), then barrier.  Returns false on timeout.
-__device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int stream, int order, int32_t *status,
+// Epilogue: wait until boundary `slot` has been published (one thread spins,
+// bounded), then barrier.  slot < 0: no wait.  Returns false on timeout.
+__device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int slot, int32_t *status,
                                            volatile int *abort_flag) {
   __shared__ int ok_flag;
   if (e.et == 0) {
     int ok = 1;
-    if (order > 0 && ld_acquire(qu.flags + stream) < order) {
+    if (slot >= 0 && ld_acquire(qu.flags + slot) == 0) {
       const long long t0 = clock64();
-      while (ld_acquire(qu.flags + stream) < order) {
+      while (ld_acquire(qu.flags + slot) == 0) {
         if (*abort_flag || clock64() - t0 > kWaitCycles) {
           if (status) atomicOr(status, KDA_ERR_DEVICE_TIMEOUT);
           *abort_flag = 1;
@@ -295,11 +388,15 @@ __device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int st
   return ok_flag != 0;
 }
 
-// Epilogue: after every thread stored its part of the slot, publish it.
-__device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int stream, int order) {
-  __threadfence();
+// Epilogue: after every thread stored its part of the slot, publish it.  The
+// barrier orders the other threads' stores before thread 0's fence, which is
+// cumulative, so one fence suffices.
+__device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int slot) {
   named_bar_sync(1, kEpi);
-  if (e.et == 0) atomicExch(qu.flags + stream, order + 1);
+  if (e.et == 0) {
+    __threadfence();
+    atomicExch(qu.flags + slot, 1);
+  }
 }
 
 }  // namespace tc

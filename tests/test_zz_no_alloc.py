@@ -13,6 +13,9 @@ This file is collected last on purpose: if it fails, a run that stops at the
 first failure has already run every other test.
 """
 import ctypes
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -23,6 +26,7 @@ from simpletrain_b200.ops import _DTYPES, _decay_fields, _desc, _ptr, status_wor
 from simpletrain_b200.workloads import custom, make_inputs
 
 pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 TOL_LOWP = 2e-2    # bf16 outputs, normwise max|x-ref|/max|ref|
 TOL_STATE = 1e-3   # fp32 final state
@@ -70,15 +74,29 @@ def test_noalloc_matches_allocating_entry_point_twice(B, H, T, D):
         assert max_rel(s.cpu(), s_ref.cpu()) <= TOL_STATE
 
 
+_OVERSIZE_CHILD = r"""
+import ctypes
+from simpletrain_b200 import _ffi
+lib = _ffi.load()
+B, H, T, D = 1, 600, 64, 128          # 600 single-chunk streams, one range each
+need = lib.kda_fwd_workspace_bytes(B, H, T, D, 64, 0)
+p = _ffi.KdaFwdParams()
+p.B, p.H, p.T, p.D, p.chunk, p.dtype = B, H, T, D, 64, _ffi.KDA_DTYPE_BF16
+before = _ffi.launch_count()
+rc = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
+print(need, rc, _ffi.launch_count() - before)
+"""
+
+
 def test_noalloc_rejects_problems_larger_than_its_scratch():
-    lib = _ffi.load()
-    B, H, T, D = 1, 300, 64, 128          # 300 (batch, head) streams at D=128
-    assert lib.kda_fwd_workspace_bytes(B, H, T, D, 64, 0) > _ffi.NOALLOC_SCRATCH_BYTES
-    q = torch.zeros(B, H, T, D, dtype=torch.bfloat16, device="cuda")
-    y = torch.empty_like(q)
-    dec = torch.full((B, H, D), 0.9, device="cuda")
-    p = _params(q, q, q, None, dec, None, y, None)
-    launches = _ffi.launch_count()
-    rc = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
+    # The scratch holds one state slot per boundary between work ranges, and by
+    # default there is one range per resident CTA, which stays far below the
+    # limit; KDA_SM100_RANGES forces one range per chunk in a child process.
+    env = dict(os.environ, KDA_SM100_RANGES="600")
+    out = subprocess.run([sys.executable, "-c", _OVERSIZE_CHILD], env=env, cwd=ROOT,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    need, rc, launched = (int(x) for x in out.stdout.split())
+    assert need > _ffi.NOALLOC_SCRATCH_BYTES
     assert rc == _ffi.KDA_ERR_WORKSPACE
-    assert _ffi.launch_count() == launches     # refused before anything was enqueued
+    assert launched == 0                       # refused before anything was enqueued
