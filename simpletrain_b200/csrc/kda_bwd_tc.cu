@@ -32,6 +32,8 @@
 #include "kda_tc_epi.cuh"
 #include "tmap.h"
 
+KDA_TRACE_DEFINE
+
 namespace kda {
 namespace {
 using namespace tc;
@@ -124,16 +126,19 @@ template <typename T, int D, bool LIT, int NS>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_fwddir_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
-                         const __grid_constant__ CUtensorMap tdy, const BwdArgs a, const Queue qu) {
+                         const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tdq,
+                         const __grid_constant__ CUtensorMap tdg, const BwdArgs a, const Queue qu) {
   using L = BwdLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
+  // tensor memory: A_QK scores and A_DP dP, then together (A_DQ) dq; A_X O; A_Y W; A_Z the carried state
+  constexpr uint32_t A_DQ = L::A_QK;
   enum {
-    QK_FULL = 2 * NS, QK_FREE, DO_FULL, W_FULL, W_FREE, S_READY, DQ_FREE, KV_FULL, P_FULL, O_FULL, O_FREE,
-    DP_FULL, DP_FREE, DPM_FULL, DQ_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
+    QK_FULL = 2 * NS, DO_FULL, W_FULL, S_READY, KV_FULL, P_FULL, DP_FULL, DPM_FULL, O_FULL, DQ_FULL, OUT_FREE,
+    UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -143,30 +148,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool want_dd = a.ddecay != nullptr;
 
   if (threadIdx.x == 0) {
+    KDA_TRACE_CTA(0, kda_globaltimer());
+    KDA_TRACE_CTA(7, kda_smid());
+  }
+  if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar(FULL + s), 1);
       mbar_init(bar(EMPTY + s), 2);
     }
-    mbar_init(bar(QK_FULL + 0), 1);
-    mbar_init(bar(QK_FULL + 1), kEpi);
-    mbar_init(bar(QK_FULL + 2), 1);
-    mbar_init(bar(QK_FULL + 3), 1);
-    mbar_init(bar(QK_FULL + 4), kEpi);
-    mbar_init(bar(QK_FULL + 5), 1);
-    mbar_init(bar(QK_FULL + 6), kEpi);
-    mbar_init(bar(QK_FULL + 7), 1);
-    mbar_init(bar(QK_FULL + 8), 1);
-    mbar_init(bar(QK_FULL + 9), 1);
-    mbar_init(bar(QK_FULL + 10), kEpi);
-    mbar_init(bar(QK_FULL + 11), 1);
-    mbar_init(bar(QK_FULL + 12), kEpi);
-    mbar_init(bar(QK_FULL + 13), 1);
-    mbar_init(bar(QK_FULL + 14), 1);
-    mbar_init(bar(QK_FULL + 15), 1);
-    mbar_init(bar(QK_FULL + 16), 1);
-    mbar_init(bar(QK_FULL + 17), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 18), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 19), 1);
+    mbar_init(bar(QK_FULL), 1);
+    mbar_init(bar(DO_FULL), 1);
+    mbar_init(bar(W_FULL), 1);
+    mbar_init(bar(S_READY), 1);  // also: W read, tensor memory holds decay^L S_{c-1}
+    mbar_init(bar(KV_FULL), 1);
+    mbar_init(bar(P_FULL), 1);
+    mbar_init(bar(DP_FULL), 1);
+    mbar_init(bar(DPM_FULL), 1);  // also: the scores and dP were read
+    mbar_init(bar(O_FULL), 1);
+    mbar_init(bar(DQ_FULL), 1);
+    mbar_init(bar(OUT_FREE), kEpi);  // O and dq were read
+    mbar_init(bar(UNIT_FULL0), 1);
+    mbar_init(bar(UNIT_FULL1), 1);
+    mbar_init(bar(UNIT_FREE0), 1 + kEpi);
+    mbar_init(bar(UNIT_FREE1), 1 + kEpi);
+    mbar_init(bar(FIN), 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -200,8 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
+          // the last chunk's O and dq were read: A_QK, A_DP, A_X free
           if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
-                     mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag)))
+                     mbar_wait(bar(OUT_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
@@ -209,24 +215,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16(tmem + L::A_QK, sdesc_k(st + L::ST_Q + off), sdesc_k(st + L::ST_K + off), id_qk, ks > 0);
           }
           mma_commit(bar(QK_FULL));
-          if (!(ok = mbar_wait(bar(DO_FULL), ph, a.status, abort_flag) &&
-                     mbar_wait(bar(W_FREE), ph ^ 1, a.status, abort_flag)))
-            break;
+          // W = Q^T dO and dP = dO V^T once dO is staged
+          if (!(ok = mbar_wait(bar(DO_FULL), ph, a.status, abort_flag))) break;
           tc_fence_after();
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
+            mma_f16(tmem + L::A_DP, sdesc_k(sb + L::DO + off), sdesc_k(st + L::ST_V + off), id_dp, ks > 0);
+          }
+          mma_commit(bar(DP_FULL));
           for (int ks = 0; ks < 4; ++ks)
             mma_f16(tmem + L::A_Y, sdesc_mn(st + L::ST_Q + ks * 2048, kTile), sdesc_mn(sb + L::DO + ks * 2048, kTile),
                     id_w, ks > 0);
           mma_commit(bar(W_FULL));
-          // S_{c-1} operand written; tensor memory holds decay^L S_{c-1}
-          if (!(ok = mbar_wait(bar(S_READY), ph, a.status, abort_flag) &&
-                     mbar_wait(bar(DQ_FREE), ph ^ 1, a.status, abort_flag)))
-            break;
+          // intra-chunk parts while the epilogue steps the state: O = P V, dq = dP K
+          if (!(ok = mbar_wait(bar(P_FULL), ph, a.status, abort_flag))) break;
+          tc_fence_after();
+          for (int ks = 0; ks < 4; ++ks)
+            mma_f16(tmem + L::A_X, sdesc_k(sb + L::P + ks * 32), sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_pv,
+                    ks > 0);
+          if (!(ok = mbar_wait(bar(DPM_FULL), ph, a.status, abort_flag))) break;
+          tc_fence_after();
+          for (int ks = 0; ks < 4; ++ks)
+            mma_f16(tmem + A_DQ, sdesc_k(sb + L::DP + ks * 32), sdesc_mn(st + L::ST_K + ks * 2048, kTile), id_dq,
+                    ks > 0);
+          // inter-chunk parts: O += Q S_{c-1}, dq += dO S_{c-1}^T, S += K^T V
+          if (!(ok = mbar_wait(bar(S_READY), ph, a.status, abort_flag))) break;
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
-            mma_f16(tmem + L::A_X, sdesc_k(st + L::ST_Q + off), sdesc_mn(sb + L::SB + ks * 2048, L::PANEL), id_qs,
-                    ks > 0);
+            mma_f16(tmem + L::A_X, sdesc_k(st + L::ST_Q + off), sdesc_mn(sb + L::SB + ks * 2048, L::PANEL), id_qs, 1);
           }
+          mma_commit(bar(O_FULL));
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
+            const uint32_t poff = (ks >> 2) * L::PANEL + (ks & 3) * 32;
+            mma_f16(tmem + A_DQ, sdesc_k(sb + L::DO + off), sdesc_k(sb + L::SB + poff), id_ds, 1);
+          }
+          mma_commit(bar(DQ_FULL));
           for (int ks = 0; ks < 4; ++ks) {
             if (LIT)
               mma_f16(tmem + L::A_Z, sdesc_k(st + L::ST_K + ks * 32), sdesc_k(st + L::ST_V + ks * 32), id_kv, 1);
@@ -235,32 +260,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                       sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_kv, 1);
           }
           mma_commit(bar(KV_FULL));
-          if (!(ok = mbar_wait(bar(P_FULL), ph, a.status, abort_flag))) break;
-          tc_fence_after();
-          for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + L::A_X, sdesc_k(sb + L::P + ks * 32), sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_pv,
-                    1);
-          mma_commit(bar(O_FULL));
-          if (!(ok = mbar_wait(bar(DP_FREE), ph ^ 1, a.status, abort_flag))) break;
-          tc_fence_after();
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
-            mma_f16(tmem + L::A_DP, sdesc_k(sb + L::DO + off), sdesc_k(st + L::ST_V + off), id_dp, ks > 0);
-          }
-          mma_commit(bar(DP_FULL));
-          if (!(ok = mbar_wait(bar(DPM_FULL), ph, a.status, abort_flag) &&
-                     mbar_wait(bar(O_FREE), ph, a.status, abort_flag)))
-            break;
-          tc_fence_after();
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
-            const uint32_t poff = (ks >> 2) * L::PANEL + (ks & 3) * 32;
-            mma_f16(tmem + L::A_X, sdesc_k(sb + L::DO + off), sdesc_k(sb + L::SB + poff), id_ds, ks > 0);
-          }
-          for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + L::A_X, sdesc_k(sb + L::DP + ks * 32), sdesc_mn(st + L::ST_K + ks * 2048, kTile), id_dq,
-                    1);
-          mma_commit(bar(DQ_FULL));
           mma_commit(bar(EMPTY + s));
         }
         if (!ok) break;
@@ -304,15 +303,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t st = sb + s * L::STAGE;
         const int t0 = 64 * c, Lc = min(64, a.T - t0);
         if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
-        // (0) dO
+        if (e.et == 0) KDA_TRACE_EVENT(0, gc);
+        // (0) dO (the DO tile's last readers were the previous chunk's MMAs)
         make_do<D, BF>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate);
         fence_async_smem();
+        if (e.et == 0 && gc > 0) {
+          // the previous chunk's dg (from its dy tile) and dq (from P / DP) stores have read smem
+          tma_store_wait_read<0>();
+          mbar_arrive(bar(EMPTY + (gc - 1) % NS));
+        }
         named_bar_sync(1, kEpi);
-        if (e.et == 0) mbar_arrive(bar(DO_FULL));
+        if (e.et == 0) {
+          mbar_arrive(bar(DO_FULL));
+          KDA_TRACE_EVENT(1, gc);
+        }
+        // (a) P, (b) dP
+        if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(5, gc);
+        tc_fence_after();
+        masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
+        if (!(ok = mbar_wait(bar(DP_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(6, gc);
+        tc_fence_after();
+        masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
+        fence_async_smem();
+        named_bar_sync(1, kEpi);
+        if (e.et == 0) {
+          mbar_arrive(bar(P_FULL));
+          mbar_arrive(bar(DPM_FULL));
+          KDA_TRACE_EVENT(7, gc);
+        }
         // (s) state step: S_{c-1} -> operand, decay^L S_{c-1} -> tensor memory,
         //     decay term <T_{c-1}, W_c>, tangent update; column slices of 32
         if (c > u.c_begin && !(ok = mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag))) break;
         if (!(ok = mbar_wait(bar(W_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(2, gc);
         tc_fence_after();
         {
           float alr[Carry<D>::NR];
@@ -321,48 +346,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (D == 128) {
             const int row = Td.row[0];
             const uint32_t pb = sb + L::SB + (uint32_t)(e.half * L::PANEL);
-            for (int sl = 0; sl < 2; ++sl) {
-              const int col0 = 64 * e.half + 32 * sl;
-              uint32_t u32[32], w32[32];
+            for (int sl = 0; sl < 4; ++sl) {  // column slices of 16
+              const int col0 = 64 * e.half + 16 * sl;
+              uint32_t u32[16], w32[16];
               if (c == u.c_begin) {
                 if (prev) {
-                  for (int q4 = 0; q4 < 8; ++q4) {
-                    const float4 v = __ldcg(prev + (8 * sl + q4) * kEpi + e.et);
+                  for (int q4 = 0; q4 < 4; ++q4) {
+                    const float4 v = __ldcg(prev + (4 * sl + q4) * kEpi + e.et);
                     u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
                     u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
                   }
                 } else if (a.s_in) {
                   const float4 *s4 = reinterpret_cast<const float4 *>(a.s_in + sbase + (size_t)row * D + col0);
-                  for (int q4 = 0; q4 < 8; ++q4) {
+                  for (int q4 = 0; q4 < 4; ++q4) {
                     const float4 v = __ldg(s4 + q4);
                     u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
                     u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
                   }
                 } else {
-                  for (int k = 0; k < 32; ++k) u32[k] = 0u;
+                  for (int k = 0; k < 16; ++k) u32[k] = 0u;
                 }
+                if (want_dd) tmem_ld_32x32b_x16(tmem + e.lane_off + L::A_Y + col0, w32);
+              } else if (want_dd) {
+                tmem_ld2_32x32b_x16(tmem + e.lane_off + L::A_Z + col0, u32, tmem + e.lane_off + L::A_Y + col0, w32);
               } else {
-                tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Z + col0, u32);
+                tmem_ld_32x32b_x16(tmem + e.lane_off + L::A_Z + col0, u32);
               }
               if (want_dd) {
-                tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Y + col0, w32);
                 float acc = 0.f;
-                for (int k = 0; k < 32; ++k) acc = fmaf(Td.x[0][32 * sl + k], __uint_as_float(w32[k]), acc);
+                for (int k = 0; k < 16; ++k) acc = fmaf(Td.x[0][16 * sl + k], __uint_as_float(w32[k]), acc);
                 dl[0] += acc;
               }
-              for (int j = 0; j < 4; ++j)
-                st_shared_v4(pb + swz(row, 32 * sl + 8 * j),
+              for (int j = 0; j < 2; ++j)
+                st_shared_v4(pb + swz(row, 16 * sl + 8 * j),
                              pack2(__uint_as_float(u32[8 * j]), __uint_as_float(u32[8 * j + 1]), BF),
                              pack2(__uint_as_float(u32[8 * j + 2]), __uint_as_float(u32[8 * j + 3]), BF),
                              pack2(__uint_as_float(u32[8 * j + 4]), __uint_as_float(u32[8 * j + 5]), BF),
                              pack2(__uint_as_float(u32[8 * j + 6]), __uint_as_float(u32[8 * j + 7]), BF));
-              for (int k = 0; k < 32; ++k) {
+              for (int k = 0; k < 16; ++k) {
                 const float sv = __uint_as_float(u32[k]);
-                Td.x[0][32 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][32 * sl + k]);
+                Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
                 u32[k] = __float_as_uint(alr[0] * sv);
               }
-              tmem_st_32x32b_x32(tmem + e.lane_off + L::A_Z + col0, u32);
+              tmem_st_32x32b_x16_nowait(tmem + e.lane_off + L::A_Z + col0, u32);
             }
+            tmem_wait_st();
           } else {
             Carry<D> Sp;
             Sp.row[0] = Td.row[0];
@@ -388,62 +416,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             Sp.tmem_store(e, tmem, L::A_Z);
           }
         }
+        if (e.et == 0) KDA_TRACE_EVENT(3, gc);
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(bar(W_FREE));
         named_bar_sync(1, kEpi);
-        if (e.et == 0) mbar_arrive(bar(S_READY));
-        // (a) P
-        if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
-        tc_fence_after();
-        masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
-        mbar_arrive(bar(QK_FREE));
-        fence_async_smem();
-        named_bar_sync(1, kEpi);
-        if (e.et == 0) mbar_arrive(bar(P_FULL));
-        // (b) O -> dg
+        if (e.et == 0) {
+          mbar_arrive(bar(S_READY));
+          KDA_TRACE_EVENT(4, gc);
+        }
+        // (c) dg = dy * O over the dy tile, then a TMA store
         if (!(ok = mbar_wait(bar(O_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(8, gc);
         tc_fence_after();
-        {
+        if (gate) {
           Frag<D / 2> fo;
           ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, fo);
-          tc_fence_before();
-          mbar_arrive(bar(O_FREE));
-          if (gate) {
-            float dg[D / 2];
-            for (int j = 0; j < D / 16; ++j)
-              for (int ee = 0; ee < 2; ++ee) {
-                const int col = (D / 2) * e.half + 8 * j + e.cq;
-                const float2 y = unpack2(ld_shared_u32(box_addr(st + L::ST_DY, e.r0 + 8 * ee, col)), BF);
-                dg[4 * j + 2 * ee] = y.x * fo.v(ee, j, 0);
-                dg[4 * j + 2 * ee + 1] = y.y * fo.v(ee, j, 1);
-              }
-            store_frag_global<D, BF>(e, dg, a.dg, b, h, t0, Lc);
+          uint32_t yv[D / 8];  // all dy loads first: the shared-memory accesses are ordered asm
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee)
+              yv[2 * j + ee] = ld_shared_u32(box_addr(st + L::ST_DY, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq));
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee) {
+              const float2 y = unpack2(yv[2 * j + ee], BF);
+              st_shared_u32(box_addr(st + L::ST_DY, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
+                            pack2(y.x * fo.v(ee, j, 0), y.y * fo.v(ee, j, 1), BF));
+            }
+          fence_async_smem();
+          named_bar_sync(1, kEpi);
+          if (e.et == 0) {
+            for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdg, st + L::ST_DY + kb * kTile, 64 * kb, t0, h, b);
+            tma_store_commit();
           }
         }
-        // (d) masked dP
-        if (!(ok = mbar_wait(bar(DP_FULL), ph, a.status, abort_flag))) break;
-        tc_fence_after();
-        masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
-        mbar_arrive(bar(DP_FREE));
-        fence_async_smem();
-        named_bar_sync(1, kEpi);  // also: every read of this stage's g / dy is done
-        if (e.et == 0) {
-          mbar_arrive(bar(DPM_FULL));
-          mbar_arrive(bar(EMPTY + s));
-        }
-        // (e) dq
+        if (e.et == 0) KDA_TRACE_EVENT(9, gc);
+        // (d) dq into the P / DP tiles (their MMAs are done), then a TMA store
         if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
         tc_fence_after();
         {
           Frag<D / 2> fd;
-          ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, fd);
+          ld_frag(tmem + e.lane_off + A_DQ + (D / 2) * e.half, fd);
           tc_fence_before();
-          mbar_arrive(bar(DQ_FREE));
-          float dq[D / 2];
-          for (int k = 0; k < D / 2; ++k) dq[k] = __uint_as_float(fd.r[k]);
-          store_frag_global<D, BF>(e, dq, a.dq, b, h, t0, Lc);
+          mbar_arrive(bar(OUT_FREE));
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee) {
+              const int row = e.r0 + 8 * ee, col = (D / 2) * e.half + 8 * j + e.cq;
+              st_shared_u32(box_addr(sb + L::P, row, col), pack2(fd.v(ee, j, 0), fd.v(ee, j, 1), BF));
+            }
         }
+        fence_async_smem();
+        named_bar_sync(1, kEpi);
+        if (e.et == 0) {
+          for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdq, sb + L::P + kb * kTile, 64 * kb, t0, h, b);
+          tma_store_commit();
+          KDA_TRACE_EVENT(10, gc);
+        }
+        if (e.et == 0) KDA_TRACE_EVENT(12, gc);
       }
       if (!ok) break;
       // unit end: the last K^T V has landed in tensor memory
@@ -484,6 +511,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
       }
     }
+  }
+  if (threadIdx.x == 64) {
+    tma_store_wait_all();  // dg / dq stores of the last chunk
+    KDA_TRACE_CTA(2, kda_globaltimer());
   }
   __syncthreads();
   if (warp == 1) {
@@ -662,19 +693,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t st = sb + s * L::STAGE;
         const int t0 = 64 * c, Lc = min(64, a.T - t0);
         if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(16, gc);
         make_do<D, BF>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate);
         fence_async_smem();
         named_bar_sync(1, kEpi);  // every read of this stage's g / dy is done
         if (e.et == 0) {
           mbar_arrive(bar(DO_FULL));
           mbar_arrive(bar(EMPTY + s));
+          KDA_TRACE_EVENT(17, gc);
         }
         // (a) P, (b) dP
         if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(18, gc);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
         mbar_arrive(bar(QK_FREE));
         if (!(ok = mbar_wait(bar(DP_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(19, gc);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
         mbar_arrive(bar(DP_FREE));
@@ -683,11 +718,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (e.et == 0) {
           mbar_arrive(bar(P_FULL));
           mbar_arrive(bar(DPM_FULL));
+          KDA_TRACE_EVENT(20, gc);
         }
         // (c) dS <- decay^L dS + Q^T dO once the inter MMAs have read dS_c
         if (!(ok = mbar_wait(bar(INTER_FULL), ph, a.status, abort_flag) &&
                    mbar_wait(bar(W_FULL), ph, a.status, abort_flag)))
           break;
+        if (e.et == 0) KDA_TRACE_EVENT(21, gc);
         tc_fence_after();
         {
           float al[Carry<D>::NR];
@@ -708,14 +745,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(bar(W_FREE));
+        if (e.et == 0) KDA_TRACE_EVENT(22, gc);
         if (k + 1 < u.c_end - u.c_begin) {
           dS.template write_operand<BF>(e, sb + L::SB);
           fence_async_smem();
           named_bar_sync(1, kEpi);
           if (e.et == 0) mbar_arrive(bar(DS_READY));
         }
+        if (e.et == 0) KDA_TRACE_EVENT(23, gc);
         // (e) dk, dv
         if (!(ok = mbar_wait(bar(DKV_FULL), ph, a.status, abort_flag))) break;
+        if (e.et == 0) KDA_TRACE_EVENT(24, gc);
         tc_fence_after();
         {
           float o[D / 2];
@@ -725,6 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < D / 2; ++kk) o[kk] = __uint_as_float(f.r[kk]);
           }
           store_frag_global<D, BF>(e, o, a.dk, b, h, t0, Lc);
+          if (e.et == 0) KDA_TRACE_EVENT(25, gc);
           {
             Frag<D / 2> f;
             ld_frag(tmem + e.lane_off + L::A_Y + (D / 2) * e.half, f);
@@ -733,6 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(bar(DKV_FREE));
           store_frag_global<D, BF>(e, o, a.dv, b, h, t0, Lc);
+          if (e.et == 0) KDA_TRACE_EVENT(26, gc);
         }
       }
       if (!ok) break;
@@ -755,11 +797,13 @@ template <typename T, int D, bool LIT, int NS>
 cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, int grid1, int grid2,
                           cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap mq, mk, mv, mg, mdy;
+  CUtensorMap mq, mk, mv, mg, mdy, mdq, mdg;
   const View gview = a.g.data ? a.g : a.q;
+  const View dgview = a.dg.data ? a.dg : a.dq;
   bool ok = make_tmap_bhtd(&mq, a.q, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mk, a.k, a.B, a.H, a.T, a.D, BF) &&
             make_tmap_bhtd(&mv, a.v, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mg, gview, a.B, a.H, a.T, a.D, BF) &&
-            make_tmap_bhtd(&mdy, a.dy, a.B, a.H, a.T, a.D, BF);
+            make_tmap_bhtd(&mdy, a.dy, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mdq, a.dq, a.B, a.H, a.T, a.D, BF) &&
+            make_tmap_bhtd(&mdg, dgview, a.B, a.H, a.T, a.D, BF);
   if (!ok) return cudaErrorInvalidValue;
   using L = BwdLayout<D, NS>;
   auto k1 = bwd_fwddir_tc_kernel<T, D, LIT, NS>;
@@ -767,7 +811,7 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  k1<<<grid1, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, mdy, a, q1);
+  k1<<<grid1, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, a, q1);
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -793,3 +837,12 @@ cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue
 }
 
 }  // namespace kda
+
+#ifdef KDA_TRACE
+extern "C" int kda_trace_copy_bwd(unsigned long long *host) {
+  return (int)cudaMemcpyFromSymbol(host, g_kda_trace, sizeof(g_kda_trace));
+}
+extern "C" int kda_trace_copy_bwd_cta(unsigned long long *host) {
+  return (int)cudaMemcpyFromSymbol(host, g_kda_trace_cta, sizeof(g_kda_trace_cta));
+}
+#endif

@@ -13,15 +13,19 @@
 //   S_c  = decay^L S_{c-1} + U_c       epilogue registers -> 16-bit smem operand
 //   y_c  = g_c * O_c                   epilogue -> global (16-byte stores)
 //
-// Warp 0 issues TMA loads (q, k, v, g) into an NS-stage ring and takes the
-// unit tickets; warp 1 owns tensor memory and one thread issues the MMAs;
-// warps 2-9 run the epilogue (two per TMEM sub-partition).  A unit starts
-// from its chain predecessor's published state and publishes its own.
+// Warp 0 takes range tickets (kda_tc_epi.cuh) and issues TMA loads of q, k, v
+// into an NS-stage ring; warp 1 owns tensor memory and one thread issues the
+// MMAs; warps 2-9 run the epilogue (two per TMEM sub-partition); warp 10
+// loads g into an NY-deep ring of tiles that the epilogue overwrites in place
+// with y = g * O and stores with TMA.  A piece starts from the initial state
+// or from the state published at its range boundary, and publishes its own
+// when it ends mid-stream.
 //
 // Pipelining: O is double-buffered in tensor memory and the epilogue runs
 // "state update of c -> store y_c -> mask P_{c+1}", so the MMAs of chunk c+1
-// (Q K^T, Q S_c, K^T V) execute while y_c is gated and stored.  y leaves
-// through a double-buffered smem tile and TMA stores.
+// (Q K^T, Q S_c, K^T V) execute while y_c is gated and stored.  The gate tile
+// of chunk c is requested NY-1 chunks ahead, which hides the load latency of
+// a saturated memory system without tying up a q/k/v stage.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -38,16 +42,24 @@ namespace kda {
 namespace {
 using namespace tc;
 
-template <int D, int NS>
+#ifndef KDA_FWD_NS
+#define KDA_FWD_NS 2  // q/k/v stages
+#endif
+#ifndef KDA_FWD_NY
+#define KDA_FWD_NY 4  // gate-in / y-out tiles
+#endif
+constexpr int kFwdThreads = kThreads + 32;  // + the gate-loading warp
+
+template <int D, int NS, int NY>
 struct FwdLayout {
   static constexpr int KB = D / 64;
   static constexpr int BOX = KB * kTile;
-  static constexpr int ST_Q = 0, ST_K = BOX, ST_V = 2 * BOX, STAGE = 3 * BOX;  // g is read from global
+  static constexpr int ST_Q = 0, ST_K = BOX, ST_V = 2 * BOX, STAGE = 3 * BOX;
   static constexpr int P = NS * STAGE;
   static constexpr int SB = P + kTile;  // S_{c-1}: KB panels of [D rows x 64]
-  static constexpr int Y = SB + KB * D * 128;  // two y staging tiles (BOX each)
-  static constexpr int BAR = Y + 2 * BOX;
-  static constexpr int NBAR = 2 * NS + 16;
+  static constexpr int Y = SB + KB * D * 128;  // NY tiles (BOX each): g in, y out
+  static constexpr int BAR = Y + NY * BOX;
+  static constexpr int NBAR = 2 * NS + 2 * NY + 16;
   static constexpr int RING = BAR + NBAR * 8;  // two (ticket, piece) entries
   static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
@@ -56,12 +68,12 @@ struct FwdLayout {
   static constexpr uint32_t TMEM_COLS = (64 + 3 * D) <= 256 ? 256 : 512;
 };
 
-template <typename T, int D, bool LIT, int NS>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int D, bool LIT, int NS, int NY>
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
                   const __grid_constant__ CUtensorMap ty, const FwdArgs a, const Queue qu) {
-  using L = FwdLayout<D, NS>;
+  using L = FwdLayout<D, NS, NY>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr int KB = L::KB;
   extern __shared__ uint8_t smem_raw[];
@@ -69,10 +81,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
   enum {
-    QK_FULL = 2 * NS, QK_FREE, S_READY, O_FREE0, O_FREE1, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0,
+    QK_FULL = 2 * NS + 2 * NY, QK_FREE, S_READY, O_FREE0, O_FREE1, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0,
     UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
   };
-  const int FULL = 0, EMPTY = NS;
+  const int FULL = 0, EMPTY = NS, GFULL = 2 * NS, GEMPTY = 2 * NS + NY;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
   volatile int *ring = reinterpret_cast<volatile int *>(smem + L::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,6 +97,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(FULL + s), 1);
       mbar_init(bar(EMPTY + s), 1);  // MMA commit
     }
+    for (int j = 0; j < NY; ++j) {
+      mbar_init(bar(GFULL + j), 1);
+      mbar_init(bar(GEMPTY + j), 1);  // the y store from the tile has read it
+    }
     mbar_init(bar(QK_FULL + 0), 1);
     mbar_init(bar(QK_FULL + 1), kEpi);
     mbar_init(bar(QK_FULL + 2), 1);
@@ -96,8 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(QK_FULL + 8), 1);
     mbar_init(bar(QK_FULL + 9), 1);
     mbar_init(bar(QK_FULL + 10), 1);
-    mbar_init(bar(QK_FULL + 11), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 12), 1 + kEpi);
+    mbar_init(bar(QK_FULL + 11), 2 + kEpi);  // unit ring slots: MMA, gate loader, epilogue
+    mbar_init(bar(QK_FULL + 12), 2 + kEpi);
     mbar_init(bar(QK_FULL + 13), 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -219,6 +235,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
     }
     __syncwarp();
+  } else if (warp == 10) {
+    // ----------------------------------------------------------- gate loader
+    if (lane == 0) {
+      if (gate) prefetch_tmap(&tg);
+      int gc = 0;
+      for (int i = 0;; ++i) {
+        if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break;
+        const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
+        mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
+        if (t >= qu.nranges) break;
+        const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
+        if (!gate) continue;
+        const int b = u.stream / a.H, h = u.stream - b * a.H;
+        bool ok = true;
+        for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
+          const int j = gc % NY, use = gc / NY;
+          if (!(ok = mbar_wait(bar(GEMPTY + j), (use & 1) ^ 1, a.status, abort_flag))) break;
+          const uint32_t yt = sb + L::Y + j * L::BOX;
+          mbar_arrive_expect_tx(bar(GFULL + j), (uint32_t)L::BOX);
+          for (int kb = 0; kb < KB; ++kb) tma_load_4d(yt + kb * kTile, &tg, bar(GFULL + j), 64 * kb, 64 * c, h, b);
+        }
+        if (!ok) break;
+      }
+      for (int d = gc - 1; d >= 0 && d >= gc - NY; --d)
+        mbar_wait(bar(GFULL + d % NY), (d / NY) & 1, a.status, abort_flag);
+    }
+    __syncwarp();
   } else {
     // ----------------------------------------------------------- epilogue
     const Epi e;
@@ -273,18 +316,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ph = gc & 1, ob = gc & 1;
         const int t0 = 64 * c, Lc = min(64, a.T - t0);
         const bool last = c + 1 == u.c_end;
-        // gate fragment for y_c straight from global memory; lands during the state update
-        uint32_t gfr[D / 8];
-        if (gate) {
-          const uint16_t *gp = reinterpret_cast<const uint16_t *>(a.g.data) + b * a.g.sb + h * a.g.sh;
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee) {
-              const int row = e.r0 + 8 * ee;
-              gfr[2 * j + ee] = row < Lc ? __ldg(reinterpret_cast<const unsigned int *>(
-                                               gp + (int64_t)(t0 + row) * a.g.st + (D / 2) * e.half + 8 * j + e.cq))
-                                         : 0u;
-            }
-        }
         // (b) S_c = decay^L S_{c-1} + U_c  (U_c's MMA follows Q S_{c-1}, so the operand is free)
         if (!(ok = mbar_wait(bar(KV_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(8, gc);
@@ -310,10 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
           mbar_arrive(bar(KV_FREE));
+          if (e.et == 0) KDA_TRACE_EVENT(17, gc);
         }
         if (!last) {
           S.template write_operand<BF>(e, sb + L::SB);
+          if (e.et == 0) KDA_TRACE_EVENT(18, gc);
           fence_async_smem();
+          if (e.et == 0) KDA_TRACE_EVENT(19, gc);
           named_bar_sync(1, kEpi);
           if (e.et == 0) {
             mbar_arrive(bar(S_READY));
@@ -328,6 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // (c) y_c = g_c * O_c  -> staging tile -> TMA store
         if (e.et == 0) KDA_TRACE_EVENT(7, gc);
+        const int j = gc % NY;
+        const uint32_t yt = sb + L::Y + j * L::BOX;
+        if (gate && !(ok = mbar_wait(bar(GFULL + j), (gc / NY) & 1, a.status, abort_flag))) break;
         if (!(ok = mbar_wait(bar(O_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(10, gc);
         tc_fence_after();
@@ -336,31 +373,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           ld_frag(tmem + e.lane_off + (ob ? L::A_O1 : L::A_O0) + (D / 2) * e.half, fo);
           tc_fence_before();
           mbar_arrive(bar(O_FREE0 + ob));
-          const uint32_t yt = sb + L::Y + ob * L::BOX;
-          if (e.et == 0) tma_store_wait_read1();  // the store that used this tile two chunks ago has read it
-          named_bar_sync(1, kEpi);
-          for (int j = 0; j < D / 16; ++j) {
-            const int col = (D / 2) * e.half + 8 * j + e.cq;
+          if (e.et == 0) KDA_TRACE_EVENT(20, gc);
+          if (!gate) {
+            // no gate tile was loaded: wait until the store that last used tile j has read it
+            if (e.et == 0) tma_store_wait_read<NY - 1>();
+            named_bar_sync(1, kEpi);
+          }
+          if (e.et == 0) KDA_TRACE_EVENT(21, gc);
+          uint32_t gv[D / 8];  // all gate loads first: the shared-memory accesses are ordered asm
+          if (gate)
+            for (int jj = 0; jj < D / 16; ++jj)
+              for (int ee = 0; ee < 2; ++ee)
+                gv[2 * jj + ee] = ld_shared_u32(box_addr(yt, e.r0 + 8 * ee, (D / 2) * e.half + 8 * jj + e.cq));
+          for (int jj = 0; jj < D / 16; ++jj)
             for (int ee = 0; ee < 2; ++ee) {
-              const int row = e.r0 + 8 * ee;
-              float o0 = fo.v(ee, j, 0), o1 = fo.v(ee, j, 1);
+              float o0 = fo.v(ee, jj, 0), o1 = fo.v(ee, jj, 1);
               if (gate) {
-                const float2 g2 = unpack2(gfr[2 * j + ee], BF);
+                const float2 g2 = unpack2(gv[2 * jj + ee], BF);
                 o0 *= g2.x;
                 o1 *= g2.y;
               }
-              st_shared_u32(box_addr(yt, row, col), pack2(o0, o1, BF));
+              // y over g, element by element
+              st_shared_u32(box_addr(yt, e.r0 + 8 * ee, (D / 2) * e.half + 8 * jj + e.cq), pack2(o0, o1, BF));
             }
-          }
+          if (e.et == 0) KDA_TRACE_EVENT(22, gc);
           fence_async_smem();
+          if (e.et == 0) KDA_TRACE_EVENT(23, gc);
           named_bar_sync(1, kEpi);
+          if (e.et == 0) KDA_TRACE_EVENT(24, gc);
           if (e.et == 0) {
             for (int kb = 0; kb < KB; ++kb) tma_store_4d(&ty, yt + kb * kTile, 64 * kb, t0, h, b);
             tma_store_commit();
+            if (gate && gc > 0) {
+              // the previous chunk's store has read its tile: hand it back to the gate loader
+              tma_store_wait_read<1>();
+              mbar_arrive(bar(GEMPTY + (gc - 1) % NY));
+            }
             KDA_TRACE_EVENT(11, gc);
           }
         }
-        // (a) P for the next chunk of the unit
+        // (a) P for the next chunk of the piece
         if (!last) ok = make_p(gc + 1);
       }
       if (!ok) break;
@@ -378,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int D, bool LIT, int NS>
+template <typename T, int D, bool LIT, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
 cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mg, my;
@@ -387,20 +439,20 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
       !make_tmap_bhtd(&mv, a.v, a.B, a.H, a.T, a.D, BF) || !make_tmap_bhtd(&mg, gview, a.B, a.H, a.T, a.D, BF) ||
       !make_tmap_bhtd(&my, a.y, a.B, a.H, a.T, a.D, BF))
     return cudaErrorInvalidValue;
-  using L = FwdLayout<D, NS>;
-  auto kern = fwd_tc_kernel<T, D, LIT, NS>;
+  using L = FwdLayout<D, NS, NY>;
+  auto kern = fwd_tc_kernel<T, D, LIT, NS, NY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
+  kern<<<grid, kFwdThreads, L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
   count_launches(1);
   return cudaGetLastError();
 }
 
-template <typename T, int D, bool LIT, int NS>
+template <typename T, int D, bool LIT, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
 int fwd_ctas_per_sm() {
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fwd_tc_kernel<T, D, LIT, NS>, kThreads,
-                                                    FwdLayout<D, NS>::SMEM) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fwd_tc_kernel<T, D, LIT, NS, NY>, kFwdThreads,
+                                                    FwdLayout<D, NS, NY>::SMEM) != cudaSuccess)
     return 1;
   return n > 0 ? n : 1;
 }
@@ -410,20 +462,20 @@ int fwd_ctas_per_sm() {
 int fwd_tc_occupancy(int D, int dtype, bool literal) {
   const bool bf = dtype == KDA_DTYPE_BF16;
   if (D == 64) {
-    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true, 3>() : fwd_ctas_per_sm<__half, 64, true, 3>();
-    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, 3>() : fwd_ctas_per_sm<__half, 64, false, 3>();
+    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true>() : fwd_ctas_per_sm<__half, 64, true>();
+    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false>() : fwd_ctas_per_sm<__half, 64, false>();
   }
-  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, 3>() : fwd_ctas_per_sm<__half, 128, false, 3>();
+  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false>() : fwd_ctas_per_sm<__half, 128, false>();
 }
 
 cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dtype, cudaStream_t st) {
   const bool bf = dtype == KDA_DTYPE_BF16;
   if (a.D == 64) {
     if (a.literal)
-      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true, 3>(a, q, grid, st) : fwd_tc_launch<__half, 64, true, 3>(a, q, grid, st);
-    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, 3>(a, q, grid, st) : fwd_tc_launch<__half, 64, false, 3>(a, q, grid, st);
+      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true>(a, q, grid, st) : fwd_tc_launch<__half, 64, true>(a, q, grid, st);
+    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false>(a, q, grid, st) : fwd_tc_launch<__half, 64, false>(a, q, grid, st);
   }
-  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, 3>(a, q, grid, st) : fwd_tc_launch<__half, 128, false, 3>(a, q, grid, st);
+  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false>(a, q, grid, st) : fwd_tc_launch<__half, 128, false>(a, q, grid, st);
 }
 
 }  // namespace kda

@@ -224,20 +224,26 @@ struct Carry {
 // dO = dy * g (or dy) into the DO tile; all 256 epilogue threads.
 template <int D, bool BF>
 __device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_t do_tile, bool gate) {
+  constexpr int N = 2 * (D / 64);  // 16-byte chunks per thread
   const int row = e.et >> 2, q4 = e.et & 3;
-  for (int ch = q4; ch < 8 * (D / 64); ch += 4) {
-    const uint32_t off = (uint32_t)((ch >> 3) * kTile) + (uint32_t)(row * 128) + ((((ch & 7) ^ (row & 7)) & 7) << 4);
-    uint4 y = ld_shared_v4(dy_tile + off);
+  uint32_t off[N];
+  uint4 y[N], g[N];
+  for (int i = 0; i < N; ++i) {  // all loads first: the shared-memory accesses are ordered asm
+    const int ch = q4 + 4 * i;
+    off[i] = (uint32_t)((ch >> 3) * kTile) + (uint32_t)(row * 128) + ((((ch & 7) ^ (row & 7)) & 7) << 4);
+    y[i] = ld_shared_v4(dy_tile + off[i]);
+    if (gate) g[i] = ld_shared_v4(g_tile + off[i]);
+  }
+  for (int i = 0; i < N; ++i) {
     if (gate) {
-      const uint4 g = ld_shared_v4(g_tile + off);
-      uint32_t *py = &y.x;
-      const uint32_t *pg = &g.x;
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = unpack2(py[i], BF), b = unpack2(pg[i], BF);
-        py[i] = pack2(a.x * b.x, a.y * b.y, BF);
+      uint32_t *py = &y[i].x;
+      const uint32_t *pg = &g[i].x;
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = unpack2(py[k], BF), b = unpack2(pg[k], BF);
+        py[k] = pack2(a.x * b.x, a.y * b.y, BF);
       }
     }
-    st_shared_v4(do_tile + off, y.x, y.y, y.z, y.w);
+    st_shared_v4(do_tile + off[i], y[i].x, y[i].y, y[i].z, y[i].w);
   }
 }
 
