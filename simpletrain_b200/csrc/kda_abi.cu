@@ -126,6 +126,10 @@ cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, i
   return cudaMemsetAsync(ws, 0, queue_header_bytes(nranges), st);
 }
 
+size_t do_bytes(int B, int H, int T, int D) {
+  return T > 0 ? align256((size_t)B * H * T * D * 2) : 0;
+}
+
 int n_chunks(int T, int chunk) { return chunk > 0 && T > 0 ? (T + chunk - 1) / chunk : 0; }
 
 }  // namespace
@@ -159,8 +163,9 @@ size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32
 size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t) {
   if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
   const int nr = n_ranges(B * H, n_chunks(T, chunk), bwd_slots());
-  // forward-direction pass: state, decay tangent, decay-gradient share; reverse pass: dS
-  return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D));
+  // forward-direction pass: state, decay tangent, decay-gradient share; reverse pass: dS;
+  // then dO = dy * g, [B][H][T][D] 16-bit, handed from the first pass to the second
+  return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D)) + do_bytes(B, H, T, D);
 }
 
 int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
@@ -202,7 +207,8 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   kda::tc::Queue q{};
   cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), nr, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(kda::launch_fwd_tc(a, q, nr, p->dtype, st));
+  const int slots = fwd_slots(p->D, literal);
+  return cuda_status(kda::launch_fwd_tc(a, q, nr < slots ? nr : slots, p->dtype, st));
 }
 
 int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
@@ -247,10 +253,13 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   const int f1 = 2 * carry_f4(p->D) + 1, f2 = carry_f4(p->D);
   kda::tc::Queue q1{}, q2{};
   void *ws2 = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, f1);
+  void *ws_do = reinterpret_cast<char *>(ws2) + queue_bytes(nr, f2);
+  a.dO = View{ws_do, (int64_t)p->H * p->T * p->D, (int64_t)p->T * p->D, p->D, 1};
   cudaError_t e = make_queue(q1, p->workspace, ns, nchunks, f1, nr, st);
   if (e == cudaSuccess) e = make_queue(q2, ws2, ns, nchunks, f2, nr, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(kda::launch_bwd_tc(a, q1, q2, nr, nr, p->dtype, st));
+  const int grid = nr < bwd_slots() ? nr : bwd_slots();  // persistent CTAs; extra ranges are taken in turn
+  return cuda_status(kda::launch_bwd_tc(a, q1, q2, grid, grid, p->dtype, st));
 }
 
 }  // extern "C"

@@ -39,6 +39,7 @@ namespace {
 using namespace tc;
 
 
+// forward-direction pass: stage = q, k, v, g, dy
 template <int D, int NS>
 struct BwdLayout {
   static constexpr int KB = D / 64;
@@ -61,6 +62,30 @@ struct BwdLayout {
   static constexpr uint32_t TMEM_COLS = 512;
 };
 
+// reverse pass: stage = q, k, v, dO (written by the forward-direction pass);
+// dk and dv leave through two staging tiles and TMA stores
+template <int D, int NS>
+struct RevLayout {
+  static constexpr int KB = D / 64;
+  static constexpr int BOX = KB * kTile;
+  static constexpr int ST_Q = 0, ST_K = BOX, ST_V = 2 * BOX, ST_DO = 3 * BOX;
+  static constexpr int STAGE = 4 * BOX;
+  static constexpr int P = NS * STAGE;
+  static constexpr int DP = P + kTile;
+  static constexpr int PANEL = D * 128;
+  static constexpr int SB = DP + kTile;
+  static constexpr int DK = SB + KB * PANEL;
+  static constexpr int DV = DK + BOX;
+  static constexpr int BAR = DV + BOX;
+  static constexpr int NBAR = 2 * NS + 20;
+  static constexpr int RING = BAR + NBAR * 8;
+  static constexpr int TMEM_SLOT = RING + 16;
+  static constexpr int ABORT = TMEM_SLOT + 8;
+  static constexpr int SMEM = ABORT + 8 + 1024;
+  static constexpr uint32_t A_QK = 0, A_DP = 64, A_X = 128, A_Y = 128 + D, A_Z = 128 + 2 * D;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
 // Piece-loop preamble shared by the MMA and epilogue roles.
 #define KDA_TAKE_UNIT(REVERSE)                                                           \
   if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break; \
@@ -69,21 +94,22 @@ struct BwdLayout {
   if (t >= qu.nranges) break;                                                            \
   const Piece u = piece_of(qu, span_of(qu, t, REVERSE), p, REVERSE);
 
-// Producer: tickets and TMA loads of q, k, v, (g), dy for every chunk of every unit.
-template <int D, int NS>
-__device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, uint32_t sb, volatile int *ring,
-                             volatile int *abort_flag, const CUtensorMap *tq, const CUtensorMap *tk,
-                             const CUtensorMap *tv, const CUtensorMap *tg, const CUtensorMap *tdy, int FULL, int EMPTY,
-                             int UNIT_FULL0, int UNIT_FREE0) {
-  using L = BwdLayout<D, NS>;
-  auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
-  const bool gate = a.g.data != nullptr;
-  prefetch_tmap(tq);
-  prefetch_tmap(tk);
-  prefetch_tmap(tv);
-  if (gate) prefetch_tmap(tg);
-  prefetch_tmap(tdy);
-  const uint32_t tx = (uint32_t)((4 + (gate ? 1 : 0)) * L::BOX);
+// Producer: tickets and TMA loads of the stage tiles for every chunk of every
+// piece.  Stage slot j (BOX bytes each) is filled from maps[j]; a null map
+// leaves its slot untouched (no gate).
+template <int D, int NS, int NT>
+__device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, uint32_t sb, int stage_bytes,
+                             volatile int *ring, volatile int *abort_flag, const CUtensorMap *const (&maps)[NT],
+                             uint32_t bar_base, int FULL, int EMPTY, int UNIT_FULL0, int UNIT_FREE0) {
+  constexpr int KB = D / 64, BOX = KB * kTile;
+  auto bar = [&](int i) { return bar_base + 8u * i; };
+  int ntiles = 0;
+  for (int j = 0; j < NT; ++j)
+    if (maps[j]) {
+      prefetch_tmap(maps[j]);
+      ++ntiles;
+    }
+  const uint32_t tx = (uint32_t)(ntiles * BOX);
   int gc = 0, i = 0;
   bool ok = true;
   while (ok) {
@@ -103,16 +129,12 @@ __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, ui
         const int c = reverse ? u.c_end - 1 - k : u.c_begin + k;
         const int s = gc % NS, use = gc / NS;
         if (!(ok = mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag))) break;
-        const uint32_t st = sb + s * L::STAGE;
+        const uint32_t st = sb + s * stage_bytes;
         mbar_arrive_expect_tx(bar(FULL + s), tx);
-        for (int kb = 0; kb < L::KB; ++kb) {
-          const int x = 64 * kb, t0 = 64 * c;
-          tma_load_4d(st + L::ST_Q + kb * kTile, tq, bar(FULL + s), x, t0, h, b);
-          tma_load_4d(st + L::ST_K + kb * kTile, tk, bar(FULL + s), x, t0, h, b);
-          tma_load_4d(st + L::ST_V + kb * kTile, tv, bar(FULL + s), x, t0, h, b);
-          if (gate) tma_load_4d(st + L::ST_G + kb * kTile, tg, bar(FULL + s), x, t0, h, b);
-          tma_load_4d(st + L::ST_DY + kb * kTile, tdy, bar(FULL + s), x, t0, h, b);
-        }
+        for (int j = 0; j < NT; ++j)
+          if (maps[j])
+            for (int kb = 0; kb < KB; ++kb)
+              tma_load_4d(st + j * BOX + kb * kTile, maps[j], bar(FULL + s), 64 * kb, 64 * c, h, b);
       }
     }
   }
@@ -127,7 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bwd_fwddir_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
                          const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tdq,
-                         const __grid_constant__ CUtensorMap tdg, const BwdArgs a, const Queue qu) {
+                         const __grid_constant__ CUtensorMap tdg, const __grid_constant__ CUtensorMap tdo,
+                         const BwdArgs a, const Queue qu) {
   using L = BwdLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
@@ -184,9 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::TMEM_SLOT);
 
   if (warp == 0) {
-    if (lane == 0)
-      bwd_producer<D, NS>(a, qu, false, sb, ring, abort_flag, &tq, &tk, &tv, &tg, &tdy, FULL, EMPTY, UNIT_FULL0,
-                          UNIT_FREE0);
+    if (lane == 0) {
+      const CUtensorMap *const maps[5] = {&tq, &tk, &tv, gate ? &tg : nullptr, &tdy};
+      bwd_producer<D, NS, 5>(a, qu, false, sb, L::STAGE, ring, abort_flag, maps, sb + L::BAR, FULL, EMPTY, UNIT_FULL0,
+                             UNIT_FREE0);
+    }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
@@ -307,14 +332,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (0) dO (the DO tile's last readers were the previous chunk's MMAs)
         make_do<D, BF>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate);
         fence_async_smem();
-        if (e.et == 0 && gc > 0) {
-          // the previous chunk's dg (from its dy tile) and dq (from P / DP) stores have read smem
-          tma_store_wait_read<0>();
-          mbar_arrive(bar(EMPTY + (gc - 1) % NS));
-        }
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
           mbar_arrive(bar(DO_FULL));
+          // dO also goes to the workspace, where the reverse pass reads it
+          for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdo, sb + L::DO + kb * kTile, 64 * kb, t0, h, b);
+          tma_store_commit();
           KDA_TRACE_EVENT(1, gc);
         }
         // (a) P, (b) dP
@@ -327,6 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
         fence_async_smem();
+        if (e.et == 0) {
+          // this chunk's dO store has read the DO tile (rewritten next chunk), and the last
+          // chunk's dg / dq stores have read its stage: hand that stage back
+          tma_store_wait_read<0>();
+          if (gc > 0) mbar_arrive(bar(EMPTY + (gc - 1) % NS));
+        }
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
           mbar_arrive(bar(P_FULL));
@@ -449,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (e.et == 0) KDA_TRACE_EVENT(9, gc);
-        // (d) dq into the P / DP tiles (their MMAs are done), then a TMA store
+        // (d) dq over the stage's gate tile (read only by the dO step), then a TMA store
         if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
         tc_fence_after();
         {
@@ -460,13 +489,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < D / 16; ++j)
             for (int ee = 0; ee < 2; ++ee) {
               const int row = e.r0 + 8 * ee, col = (D / 2) * e.half + 8 * j + e.cq;
-              st_shared_u32(box_addr(sb + L::P, row, col), pack2(fd.v(ee, j, 0), fd.v(ee, j, 1), BF));
+              st_shared_u32(box_addr(st + L::ST_G, row, col), pack2(fd.v(ee, j, 0), fd.v(ee, j, 1), BF));
             }
         }
         fence_async_smem();
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
-          for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdq, sb + L::P + kb * kTile, 64 * kb, t0, h, b);
+          for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdq, st + L::ST_G + kb * kTile, 64 * kb, t0, h, b);
           tma_store_commit();
           KDA_TRACE_EVENT(10, gc);
         }
@@ -529,47 +558,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T, int D, bool LIT, int NS>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_revdir_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
-                         const __grid_constant__ CUtensorMap tdy, const BwdArgs a, const Queue qu) {
-  using L = BwdLayout<D, NS>;
+                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                         const __grid_constant__ CUtensorMap tdk, const __grid_constant__ CUtensorMap tdv,
+                         const BwdArgs a, const Queue qu) {
+  using L = RevLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
+  // tensor memory: A_QK scores, A_DP dP, A_X dk, A_Y dv, A_Z W = Q^T dO
   enum {
-    QK_FULL = 2 * NS, QK_FREE, DO_FULL, DP_FULL, DP_FREE, W_FULL, W_FREE, DS_READY, DKV_FREE, INTER_FULL, P_FULL,
-    DPM_FULL, DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
+    QK_FULL = 2 * NS, QK_FREE, DP_FULL, DP_FREE, W_FULL, W_FREE, DS_READY, DKV_FREE, INTER_FULL, P_FULL, DPM_FULL,
+    DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
   volatile int *ring = reinterpret_cast<volatile int *>(smem + L::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool gate = a.g.data != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(bar(FULL + s), 1);
-      mbar_init(bar(EMPTY + s), 2);
+      mbar_init(bar(EMPTY + s), 1);  // MMA commit (the epilogue reads nothing from the stage)
     }
-    mbar_init(bar(QK_FULL + 0), 1);
-    mbar_init(bar(QK_FULL + 1), kEpi);
-    mbar_init(bar(QK_FULL + 2), 1);
-    mbar_init(bar(QK_FULL + 3), 1);
-    mbar_init(bar(QK_FULL + 4), kEpi);
-    mbar_init(bar(QK_FULL + 5), 1);
-    mbar_init(bar(QK_FULL + 6), kEpi);
-    mbar_init(bar(QK_FULL + 7), 1);
-    mbar_init(bar(QK_FULL + 8), kEpi);
-    mbar_init(bar(QK_FULL + 9), 1);
-    mbar_init(bar(QK_FULL + 10), 1);
-    mbar_init(bar(QK_FULL + 11), 1);
-    mbar_init(bar(QK_FULL + 12), 1);
-    mbar_init(bar(QK_FULL + 13), 1);
-    mbar_init(bar(QK_FULL + 14), 1);
-    mbar_init(bar(QK_FULL + 15), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 16), 1 + kEpi);
-    mbar_init(bar(QK_FULL + 17), 1);
+    mbar_init(bar(QK_FULL), 1);
+    mbar_init(bar(QK_FREE), kEpi);
+    mbar_init(bar(DP_FULL), 1);
+    mbar_init(bar(DP_FREE), kEpi);
+    mbar_init(bar(W_FULL), 1);
+    mbar_init(bar(W_FREE), kEpi);
+    mbar_init(bar(DS_READY), 1);
+    mbar_init(bar(DKV_FREE), kEpi);
+    mbar_init(bar(INTER_FULL), 1);
+    mbar_init(bar(P_FULL), 1);
+    mbar_init(bar(DPM_FULL), 1);
+    mbar_init(bar(DKV_FULL), 1);
+    mbar_init(bar(UNIT_FULL0), 1);
+    mbar_init(bar(UNIT_FULL1), 1);
+    mbar_init(bar(UNIT_FREE0), 1 + kEpi);
+    mbar_init(bar(UNIT_FREE1), 1 + kEpi);
+    mbar_init(bar(FIN), 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -582,9 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::TMEM_SLOT);
 
   if (warp == 0) {
-    if (lane == 0)
-      bwd_producer<D, NS>(a, qu, true, sb, ring, abort_flag, &tq, &tk, &tv, &tg, &tdy, FULL, EMPTY, UNIT_FULL0,
-                          UNIT_FREE0);
+    if (lane == 0) {
+      const CUtensorMap *const maps[4] = {&tq, &tk, &tv, &tdo};
+      bwd_producer<D, NS, 4>(a, qu, true, sb, L::STAGE, ring, abort_flag, maps, sb + L::BAR, FULL, EMPTY, UNIT_FULL0,
+                             UNIT_FREE0);
+    }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
@@ -610,19 +641,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16(tmem + L::A_QK, sdesc_k(st + L::ST_Q + off), sdesc_k(st + L::ST_K + off), id_qk, ks > 0);
           }
           mma_commit(bar(QK_FULL));
-          if (!(ok = mbar_wait(bar(DO_FULL), ph, a.status, abort_flag) &&
-                     mbar_wait(bar(DP_FREE), ph ^ 1, a.status, abort_flag) &&
+          if (!(ok = mbar_wait(bar(DP_FREE), ph ^ 1, a.status, abort_flag) &&
                      mbar_wait(bar(W_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
-            mma_f16(tmem + L::A_DP, sdesc_k(sb + L::DO + off), sdesc_k(st + L::ST_V + off), id_dp, ks > 0);
+            mma_f16(tmem + L::A_DP, sdesc_k(st + L::ST_DO + off), sdesc_k(st + L::ST_V + off), id_dp, ks > 0);
           }
           mma_commit(bar(DP_FULL));
           for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + L::A_Z, sdesc_mn(st + L::ST_Q + ks * 2048, kTile), sdesc_mn(sb + L::DO + ks * 2048, kTile),
-                    id_w, ks > 0);
+            mma_f16(tmem + L::A_Z, sdesc_mn(st + L::ST_Q + ks * 2048, kTile),
+                    sdesc_mn(st + L::ST_DO + ks * 2048, kTile), id_w, ks > 0);
           mma_commit(bar(W_FULL));
           if (!(ok = mbar_wait(bar(DS_READY), ph, a.status, abort_flag) &&
                      mbar_wait(bar(DKV_FREE), ph ^ 1, a.status, abort_flag)))
@@ -652,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ks = 0; ks < 4; ++ks) {
             mma_f16(tmem + L::A_X, sdesc_mn(sb + L::DP + ks * 2048, kTile), sdesc_mn(st + L::ST_Q + ks * 2048, kTile),
                     id_t, 1);
-            mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::P + ks * 2048, kTile), sdesc_mn(sb + L::DO + ks * 2048, kTile),
+            mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::P + ks * 2048, kTile), sdesc_mn(st + L::ST_DO + ks * 2048, kTile),
                     id_t, 1);
           }
           mma_commit(bar(DKV_FULL));
@@ -689,19 +719,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
         const int c = u.c_end - 1 - k;
-        const int s = gc % NS, use = gc / NS, ph = gc & 1;
-        const uint32_t st = sb + s * L::STAGE;
+        const int ph = gc & 1;
         const int t0 = 64 * c, Lc = min(64, a.T - t0);
-        if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
-        if (e.et == 0) KDA_TRACE_EVENT(16, gc);
-        make_do<D, BF>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate);
-        fence_async_smem();
-        named_bar_sync(1, kEpi);  // every read of this stage's g / dy is done
-        if (e.et == 0) {
-          mbar_arrive(bar(DO_FULL));
-          mbar_arrive(bar(EMPTY + s));
-          KDA_TRACE_EVENT(17, gc);
-        }
         // (a) P, (b) dP
         if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(18, gc);
@@ -714,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
         mbar_arrive(bar(DP_FREE));
         fence_async_smem();
+        if (e.et == 0) tma_store_wait_read<0>();  // the last chunk's dk / dv stores have read their tiles
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
           mbar_arrive(bar(P_FULL));
@@ -753,28 +773,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (e.et == 0) mbar_arrive(bar(DS_READY));
         }
         if (e.et == 0) KDA_TRACE_EVENT(23, gc);
-        // (e) dk, dv
+        // (e) dk, dv -> staging tiles -> TMA stores
         if (!(ok = mbar_wait(bar(DKV_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(24, gc);
         tc_fence_after();
         {
-          float o[D / 2];
-          {
-            Frag<D / 2> f;
-            ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, f);
-            for (int kk = 0; kk < D / 2; ++kk) o[kk] = __uint_as_float(f.r[kk]);
-          }
-          store_frag_global<D, BF>(e, o, a.dk, b, h, t0, Lc);
-          if (e.et == 0) KDA_TRACE_EVENT(25, gc);
-          {
-            Frag<D / 2> f;
-            ld_frag(tmem + e.lane_off + L::A_Y + (D / 2) * e.half, f);
-            for (int kk = 0; kk < D / 2; ++kk) o[kk] = __uint_as_float(f.r[kk]);
-          }
+          Frag<D / 2> f;
+          ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, f);
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee)
+              st_shared_u32(box_addr(sb + L::DK, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
+                            pack2(f.v(ee, j, 0), f.v(ee, j, 1), BF));
+        }
+        if (e.et == 0) KDA_TRACE_EVENT(25, gc);
+        {
+          Frag<D / 2> f;
+          ld_frag(tmem + e.lane_off + L::A_Y + (D / 2) * e.half, f);
           tc_fence_before();
           mbar_arrive(bar(DKV_FREE));
-          store_frag_global<D, BF>(e, o, a.dv, b, h, t0, Lc);
-          if (e.et == 0) KDA_TRACE_EVENT(26, gc);
+          for (int j = 0; j < D / 16; ++j)
+            for (int ee = 0; ee < 2; ++ee)
+              st_shared_u32(box_addr(sb + L::DV, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
+                            pack2(f.v(ee, j, 0), f.v(ee, j, 1), BF));
+        }
+        fence_async_smem();
+        named_bar_sync(1, kEpi);
+        if (e.et == 0) {
+          for (int kb = 0; kb < L::KB; ++kb) {
+            tma_store_4d(&tdk, sb + L::DK + kb * kTile, 64 * kb, t0, h, b);
+            tma_store_4d(&tdv, sb + L::DV + kb * kTile, 64 * kb, t0, h, b);
+          }
+          tma_store_commit();
+          KDA_TRACE_EVENT(26, gc);
         }
       }
       if (!ok) break;
@@ -785,6 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         dS.store_rm(e, a.ds_in + sbase);
       }
     }
+    if (e.et == 0) tma_store_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -797,25 +828,25 @@ template <typename T, int D, bool LIT, int NS>
 cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, int grid1, int grid2,
                           cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap mq, mk, mv, mg, mdy, mdq, mdg;
+  CUtensorMap mq, mk, mv, mg, mdy, mdq, mdg, mdo, mdk, mdv;
   const View gview = a.g.data ? a.g : a.q;
   const View dgview = a.dg.data ? a.dg : a.dq;
-  bool ok = make_tmap_bhtd(&mq, a.q, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mk, a.k, a.B, a.H, a.T, a.D, BF) &&
-            make_tmap_bhtd(&mv, a.v, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mg, gview, a.B, a.H, a.T, a.D, BF) &&
-            make_tmap_bhtd(&mdy, a.dy, a.B, a.H, a.T, a.D, BF) && make_tmap_bhtd(&mdq, a.dq, a.B, a.H, a.T, a.D, BF) &&
-            make_tmap_bhtd(&mdg, dgview, a.B, a.H, a.T, a.D, BF);
+  auto map = [&](CUtensorMap *m, const View &v) { return make_tmap_bhtd(m, v, a.B, a.H, a.T, a.D, BF); };
+  const bool ok = map(&mq, a.q) && map(&mk, a.k) && map(&mv, a.v) && map(&mg, gview) && map(&mdy, a.dy) &&
+                  map(&mdq, a.dq) && map(&mdg, dgview) && map(&mdo, a.dO) && map(&mdk, a.dk) && map(&mdv, a.dv);
   if (!ok) return cudaErrorInvalidValue;
-  using L = BwdLayout<D, NS>;
+  using L1 = BwdLayout<D, NS>;
+  using L2 = RevLayout<D, NS>;
   auto k1 = bwd_fwddir_tc_kernel<T, D, LIT, NS>;
   auto k2 = bwd_revdir_tc_kernel<T, D, LIT, NS>;
-  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L1::SMEM);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L2::SMEM);
   if (e != cudaSuccess) return e;
-  k1<<<grid1, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, a, q1);
+  k1<<<grid1, kThreads, L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  k2<<<grid2, kThreads, L::SMEM, st>>>(mq, mk, mv, mg, mdy, a, q2);
+  k2<<<grid2, kThreads, L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
   count_launches(1);
   return cudaGetLastError();
 }

@@ -39,6 +39,7 @@ struct BwdArgs {
   int B, H, T, D, C;
   int literal;
   View q, k, v, g, dy, dq, dk, dv, dg;
+  View dO;  // workspace [B][H][T][D] 16-bit: dy * g, written by the forward-direction pass
   DecaySrc decay;
   const float *s_in;
   const float *ds_out;
