@@ -113,9 +113,28 @@ size_t queue_bytes(int nranges, int slot_f4) {
   return queue_header_bytes(nranges) + ((size_t)nranges + 1) * slot_f4 * kda::tc::kEpi * 16;
 }
 
-// Lay a queue over `ws` and clear its header on the stream.
-cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, int slot_f4, int nranges,
-                       cudaStream_t st) {
+// Whether some range lies strictly inside one stream (starts and ends
+// mid-stream): then the carry would pass through a chain of ranges, and the
+// ranges' aggregates are precomputed so each link costs only a combine.
+bool has_middle(int nstreams, int nchunks, int nranges) {
+  if (nchunks <= 0 || nranges <= 0) return false;
+  const long long n = (long long)nstreams * nchunks;
+  for (int r = 0; r < nranges; ++r) {
+    const long long lo = n * r / nranges, hi = n * (r + 1) / nranges;
+    const long long s0 = lo / nchunks, s1 = (hi - 1) / nchunks;
+    if (s0 == s1 && lo - s0 * nchunks > 0 && hi - s1 * nchunks < nchunks) return true;
+  }
+  return false;
+}
+
+// aggregate buffer of one queue: nranges x agg_f4 x 256 float4 (only with middle ranges)
+size_t agg_bytes(int nstreams, int nchunks, int nranges, int agg_f4) {
+  return has_middle(nstreams, nchunks, nranges) ? (size_t)nranges * agg_f4 * kda::tc::kEpi * 16 : 0;
+}
+
+// Lay a queue (and its aggregates at `agg`, if any) over `ws` and clear its header on the stream.
+cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, int slot_f4, int nranges, void *agg,
+                       int agg_f4, cudaStream_t st) {
   q.ticket = reinterpret_cast<int *>(ws);
   q.flags = reinterpret_cast<int *>(reinterpret_cast<char *>(ws) + 16);
   q.slots = reinterpret_cast<float4 *>(reinterpret_cast<char *>(ws) + queue_header_bytes(nranges));
@@ -123,6 +142,8 @@ cudaError_t make_queue(kda::tc::Queue &q, void *ws, int nstreams, int nchunks, i
   q.nstreams = nstreams;
   q.nchunks = nchunks;
   q.nranges = nranges;
+  q.agg = has_middle(nstreams, nchunks, nranges) ? reinterpret_cast<float4 *>(agg) : nullptr;
+  q.agg_f4 = agg_f4;
   return cudaMemsetAsync(ws, 0, queue_header_bytes(nranges), st);
 }
 
@@ -156,16 +177,18 @@ const char *kda_status_string(int32_t s) {
 
 size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t flags) {
   if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
-  const int nr = n_ranges(B * H, n_chunks(T, chunk), fwd_slots(D, (flags & KDA_FLAG_LITERAL) != 0));
-  return queue_bytes(nr, carry_f4(D));
+  const int nc = n_chunks(T, chunk), nr = n_ranges(B * H, nc, fwd_slots(D, (flags & KDA_FLAG_LITERAL) != 0));
+  return queue_bytes(nr, carry_f4(D)) + agg_bytes(B * H, nc, nr, carry_f4(D));
 }
 
 size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t) {
   if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
-  const int nr = n_ranges(B * H, n_chunks(T, chunk), bwd_slots());
+  const int nc = n_chunks(T, chunk), nr = n_ranges(B * H, nc, bwd_slots());
   // forward-direction pass: state, decay tangent, decay-gradient share; reverse pass: dS;
-  // then dO = dy * g, [B][H][T][D] 16-bit, handed from the first pass to the second
-  return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D)) + do_bytes(B, H, T, D);
+  // then dO = dy * g, [B][H][T][D] 16-bit, handed from the first pass to the second;
+  // then the middle-range aggregates of both passes
+  return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D)) + do_bytes(B, H, T, D) +
+         agg_bytes(B * H, nc, nr, 2 * carry_f4(D)) + agg_bytes(B * H, nc, nr, carry_f4(D));
 }
 
 int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
@@ -205,7 +228,8 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   const int ns = p->B * p->H, nchunks = n_chunks(p->T, p->chunk);
   const int nr = n_ranges(ns, nchunks, fwd_slots(p->D, literal));
   kda::tc::Queue q{};
-  cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), nr, st);
+  void *agg = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, carry_f4(p->D));
+  cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), nr, agg, carry_f4(p->D), st);
   if (e != cudaSuccess) return cuda_status(e);
   const int slots = fwd_slots(p->D, literal);
   return cuda_status(kda::launch_fwd_tc(a, q, nr < slots ? nr : slots, p->dtype, st));
@@ -252,11 +276,13 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   const int nr = n_ranges(ns, nchunks, bwd_slots());
   const int f1 = 2 * carry_f4(p->D) + 1, f2 = carry_f4(p->D);
   kda::tc::Queue q1{}, q2{};
-  void *ws2 = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, f1);
-  void *ws_do = reinterpret_cast<char *>(ws2) + queue_bytes(nr, f2);
+  char *ws2 = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, f1);
+  char *ws_do = ws2 + queue_bytes(nr, f2);
+  char *agg1 = ws_do + do_bytes(p->B, p->H, p->T, p->D);
+  char *agg2 = agg1 + agg_bytes(ns, nchunks, nr, 2 * carry_f4(p->D));
   a.dO = View{ws_do, (int64_t)p->H * p->T * p->D, (int64_t)p->T * p->D, p->D, 1};
-  cudaError_t e = make_queue(q1, p->workspace, ns, nchunks, f1, nr, st);
-  if (e == cudaSuccess) e = make_queue(q2, ws2, ns, nchunks, f2, nr, st);
+  cudaError_t e = make_queue(q1, p->workspace, ns, nchunks, f1, nr, agg1, 2 * carry_f4(p->D), st);
+  if (e == cudaSuccess) e = make_queue(q2, ws2, ns, nchunks, f2, nr, agg2, carry_f4(p->D), st);
   if (e != cudaSuccess) return cuda_status(e);
   const int grid = nr < bwd_slots() ? nr : bwd_slots();  // persistent CTAs; extra ranges are taken in turn
   return cuda_status(kda::launch_bwd_tc(a, q1, q2, grid, grid, p->dtype, st));

@@ -1,0 +1,233 @@
+// Range aggregates for long streams (sm_100a, tcgen05 + TMEM + TMA).
+//
+// When a (batch, head) stream is longer than one work range, the ranges in
+// its middle both wait for an entry carry and publish an exit carry.  The
+// carry recurrences are linear with a diagonal (per key channel) decay, so a
+// middle range's exit carry is
+//
+//   S_out = A S_in + S_loc,         A = decay^(64 n)   (n full chunks)
+//   T_out = A T_in + 64 n A S_in + T_loc               (decay tangent)
+//   dS_out = A dS_in + dS_loc                          (reverse pass)
+//
+// where the _loc terms are the same recurrences run from zero over the
+// range's chunks.  This kernel computes them for every middle range (one CTA
+// per range, all in parallel), so the main kernels can publish a middle
+// range's exit carry as soon as its entry carry arrives instead of after the
+// range's full work (kernels/kda_kernel.py:292-295 is the recurrence).
+//
+//   MODE 0  S_loc from K, V            (forward)
+//   MODE 1  S_loc, T_loc from K, V     (backward, forward direction)
+//   MODE 2  dS_loc from Q, dO          (backward, reverse direction)
+//
+// Warp 0 loads the two tiles of each chunk into a ring, warp 1 issues one
+// UMMA per chunk (K^T V, literal K V^T, or Q^T dO) into one of two TMEM
+// accumulators, warps 2-9 fold it into the fp32 carry in registers.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "kda_internal.h"
+#include "kda_tc_epi.cuh"
+#include "tmap.h"
+
+namespace kda {
+namespace {
+using namespace tc;
+
+template <int D, int NS>
+struct AggLayout {
+  static constexpr int KB = D / 64;
+  static constexpr int BOX = KB * kTile;
+  static constexpr int ST_A = 0, ST_B = BOX, STAGE = 2 * BOX;
+  static constexpr int BAR = NS * STAGE;
+  static constexpr int NBAR = 2 * NS + 8;
+  static constexpr int TMEM_SLOT = BAR + NBAR * 8;
+  static constexpr int ABORT = TMEM_SLOT + 8;
+  static constexpr int SMEM = ABORT + 8 + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * D <= 128 ? 128 : 256;  // two accumulators of D columns
+};
+
+template <typename T, int D, bool LIT, int MODE, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    agg_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const AggArgs a,
+                  const Queue qu) {
+  using L = AggLayout<D, NS>;
+  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool REV = MODE == 2;
+  // this CTA's range; only middle ranges (one piece, both ends mid-stream) have work
+  const Span sp = span_of(qu, REV ? qu.nranges - 1 - (int)blockIdx.x : (int)blockIdx.x, REV);
+  if (sp.npieces() != 1 || sp.c0 == 0 || sp.c1 == qu.nchunks) return;
+  const int stream = sp.s0, c_begin = sp.c0, c_end = sp.c1, n = c_end - c_begin;
+  const int b = stream / a.H, h = stream - b * a.H;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
+  enum { ACC_FULL = 2 * NS, ACC_FREE = ACC_FULL + 2, FIN = ACC_FREE + 2 };
+  const int FULL = 0, EMPTY = NS;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(FULL + s), 1);
+      mbar_init(bar(EMPTY + s), 1);
+    }
+    mbar_init(bar(ACC_FULL + 0), 1);
+    mbar_init(bar(ACC_FULL + 1), 1);
+    mbar_init(bar(ACC_FREE + 0), kEpi);
+    mbar_init(bar(ACC_FREE + 1), kEpi);
+    mbar_init(bar(FIN), 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(sb + L::TMEM_SLOT, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::TMEM_SLOT);
+  auto chunk_of = [&](int k) { return REV ? c_end - 1 - k : c_begin + k; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&ta);
+      prefetch_tmap(&tb);
+      int k = 0;
+      for (; k < n; ++k) {
+        const int s = k % NS, use = k / NS, c = chunk_of(k);
+        if (!mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag)) break;
+        const uint32_t st = sb + s * L::STAGE;
+        mbar_arrive_expect_tx(bar(FULL + s), (uint32_t)(2 * L::BOX));
+        for (int kb = 0; kb < L::KB; ++kb) {
+          tma_load_4d(st + L::ST_A + kb * kTile, &ta, bar(FULL + s), 64 * kb, 64 * c, h, b);
+          tma_load_4d(st + L::ST_B + kb * kTile, &tb, bar(FULL + s), 64 * kb, 64 * c, h, b);
+        }
+      }
+      for (int d = k - 1; d >= 0 && d >= k - NS; --d) mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // forward modes: K^T V (literal: K V^T); reverse: Q^T dO
+      const uint32_t id = (LIT && !REV) ? idesc_f16(64, 64, BF, false, false) : idesc_f16(D, D, BF, true, true);
+      for (int k = 0; k < n; ++k) {
+        const int s = k % NS, use = k / NS, buf = k & 1;
+        const uint32_t st = sb + s * L::STAGE;
+        if (!(mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+              mbar_wait(bar(ACC_FREE + buf), ((k >> 1) & 1) ^ 1, a.status, abort_flag)))
+          break;
+        tc_fence_after();
+        for (int ks = 0; ks < 4; ++ks) {
+          if (LIT && !REV)
+            mma_f16(tmem + buf * D, sdesc_k(st + L::ST_A + ks * 32), sdesc_k(st + L::ST_B + ks * 32), id, ks > 0);
+          else
+            mma_f16(tmem + buf * D, sdesc_mn(st + L::ST_A + ks * 2048, kTile), sdesc_mn(st + L::ST_B + ks * 2048, kTile),
+                    id, ks > 0);
+        }
+        mma_commit(bar(ACC_FULL + buf));
+        mma_commit(bar(EMPTY + s));
+      }
+      mma_commit(bar(FIN));
+      mbar_wait(bar(FIN), 0, a.status, abort_flag);
+    }
+    __syncwarp();
+  } else {
+    const Epi e;
+    Carry<D> S, Tn;
+    S.init_rows(e);
+    S.zero();
+    Tn.row[0] = S.row[0];
+    Tn.row[Carry<D>::NR - 1] = S.row[Carry<D>::NR - 1];
+    Tn.zero();
+    float al[Carry<D>::NR];
+    for (int r = 0; r < Carry<D>::NR; ++r) al[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
+    bool ok = true;
+    for (int k = 0; k < n && ok; ++k) {
+      const int buf = k & 1;
+      if (!(ok = mbar_wait(bar(ACC_FULL + buf), (k >> 1) & 1, a.status, abort_flag))) break;
+      tc_fence_after();
+      if (D == 128) {
+        for (int sl = 0; sl < 4; ++sl) {  // column slices of 16
+          uint32_t u[16];
+          tmem_ld_32x32b_x16(tmem + e.lane_off + buf * D + 64 * e.half + 16 * sl, u);
+          for (int i = 0; i < 16; ++i) {
+            float &sv = S.x[0][16 * sl + i];
+            if (MODE == 1) Tn.x[0][16 * sl + i] = al[0] * fmaf(64.f, sv, Tn.x[0][16 * sl + i]);  // T <- a (T + L S)
+            sv = fmaf(al[0], sv, __uint_as_float(u[i]));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(bar(ACC_FREE + buf));
+      } else {
+        Carry<D> U;
+        U.row[0] = S.row[0];
+        U.row[Carry<D>::NR - 1] = S.row[Carry<D>::NR - 1];
+        U.tmem_load(e, tmem, buf * D);
+        tc_fence_before();
+        mbar_arrive(bar(ACC_FREE + buf));
+        for (int r = 0; r < Carry<D>::NR; ++r)
+          for (int i = 0; i < Carry<D>::NV; ++i) {
+            if (MODE == 1) Tn.x[r][i] = al[r] * fmaf(64.f, S.x[r][i], Tn.x[r][i]);  // T <- a (T + L S_prev)
+            S.x[r][i] = fmaf(al[r], S.x[r][i], U.x[r][i]);
+          }
+      }
+    }
+    if (ok) {
+      float4 *dst = a.agg + (size_t)sp.r * a.agg_f4 * kEpi;
+      S.store_slot(e, dst);
+      if (MODE == 1) Tn.store_slot(e, dst + (Carry<D>::FLOATS / 4) * kEpi);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+template <typename T, int D, bool LIT, int MODE>
+cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Queue &q, cudaStream_t st) {
+  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int NS = 4;
+  CUtensorMap ma, mb;
+  if (!make_tmap_bhtd(&ma, va, a.B, a.H, a.T, D, BF) || !make_tmap_bhtd(&mb, vb, a.B, a.H, a.T, D, BF))
+    return cudaErrorInvalidValue;
+  using L = AggLayout<D, NS>;
+  auto kern = agg_tc_kernel<T, D, LIT, MODE, NS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<q.nranges, kThreads, L::SMEM, st>>>(ma, mb, a, q);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t agg_dispatch(const AggArgs &a, const View &va, const View &vb, const Queue &q, int dtype,
+                         cudaStream_t st) {
+  const bool bf = dtype == KDA_DTYPE_BF16;
+  if (a.D == 64) {
+    if (a.literal)
+      return bf ? agg_launch<__nv_bfloat16, 64, true, MODE>(a, va, vb, q, st)
+                : agg_launch<__half, 64, true, MODE>(a, va, vb, q, st);
+    return bf ? agg_launch<__nv_bfloat16, 64, false, MODE>(a, va, vb, q, st)
+              : agg_launch<__half, 64, false, MODE>(a, va, vb, q, st);
+  }
+  return bf ? agg_launch<__nv_bfloat16, 128, false, MODE>(a, va, vb, q, st)
+            : agg_launch<__half, 128, false, MODE>(a, va, vb, q, st);
+}
+
+}  // namespace
+
+cudaError_t launch_agg_tc(int mode, const AggArgs &a, const View &va, const View &vb, const tc::Queue &q, int dtype,
+                          cudaStream_t st) {
+  if (mode == 0) return agg_dispatch<0>(a, va, vb, q, dtype, st);
+  if (mode == 1) return agg_dispatch<1>(a, va, vb, q, dtype, st);
+  return agg_dispatch<2>(a, va, vb, q, dtype, st);
+}
+
+}  // namespace kda

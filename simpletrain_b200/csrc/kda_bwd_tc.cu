@@ -307,20 +307,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       const float4 *prev = u.wait_slot >= 0 ? slot_ptr(qu, u.wait_slot) : nullptr;
       constexpr int CF4 = Carry<D>::FLOATS / 4;  // float4 per thread of one carry
-      if (prev) {
-        Td.load_slot(e, prev + CF4 * kEpi);
-        const float4 v = __ldcg(prev + 2 * CF4 * kEpi + e.et);
-        dl[0] = v.x;
-        dl[Carry<D>::NR - 1] = (Carry<D>::NR > 1) ? v.y : v.x;
-      } else {
-        Td.zero();
-        for (int r = 0; r < Carry<D>::NR; ++r) dl[r] = 0.f;
-      }
+      // the previous range's decay-gradient share is added at the end of the piece
+      for (int r = 0; r < Carry<D>::NR; ++r) dl[r] = 0.f;
+      if (prev) Td.load_slot(e, prev + CF4 * kEpi);
+      else Td.zero();
       float af[Carry<D>::NR], at[Carry<D>::NR];
       const int Ltail = a.T - (qu.nchunks - 1) * 64;
       for (int r = 0; r < Carry<D>::NR; ++r) {
         af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
+      }
+      const bool early = u.early(qu);
+      if (early) {
+        // middle range: exit state and tangent follow from the entry ones and the aggregate:
+        // S_out = A S_in + S_loc, T_out = A T_in + 64 n A S_in + T_loc
+        const int n = u.c_end - u.c_begin;
+        float A[Carry<D>::NR], An[Carry<D>::NR];
+        for (int r = 0; r < Carry<D>::NR; ++r) {
+          A[r] = powf(af[r], (float)n);
+          An[r] = 64.f * (float)n * A[r];
+        }
+        const float4 *ag = agg_ptr(qu, u.range);
+        float4 *dst = slot_ptr(qu, u.pub_slot);
+        const float *ft = &Td.x[0][0];
+        for (int i4 = 0; i4 < CF4; ++i4) {  // one float4 of S and of T at a time
+          const int r = (4 * i4) / Carry<D>::NV;
+          const float4 sv = __ldcg(prev + i4 * kEpi + e.et);
+          const float4 gs = __ldcg(ag + i4 * kEpi + e.et);
+          const float4 gt = __ldcg(ag + (CF4 + i4) * kEpi + e.et);
+          __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
+                                                     fmaf(A[r], sv.z, gs.z), fmaf(A[r], sv.w, gs.w)));
+          __stcg(dst + (CF4 + i4) * kEpi + e.et,
+                 make_float4(fmaf(A[r], ft[4 * i4], fmaf(An[r], sv.x, gt.x)),
+                             fmaf(A[r], ft[4 * i4 + 1], fmaf(An[r], sv.y, gt.y)),
+                             fmaf(A[r], ft[4 * i4 + 2], fmaf(An[r], sv.z, gt.z)),
+                             fmaf(A[r], ft[4 * i4 + 3], fmaf(An[r], sv.w, gt.w))));
+        }
+        chain_publish(e, qu, u.pub_slot, 1);
       }
       bool ok = true;
       for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
@@ -502,22 +525,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (e.et == 0) KDA_TRACE_EVENT(12, gc);
       }
       if (!ok) break;
-      // unit end: the last K^T V has landed in tensor memory
+      // piece end: the last K^T V has landed in tensor memory
       if (!mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag)) break;
       tc_fence_after();
+      if (want_dd && prev) {
+        // the previous range's share of the decay gradient (that range runs in parallel)
+        if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag, 2)) break;
+        const float4 v = __ldcg(prev + 2 * CF4 * kEpi + e.et);
+        dl[0] += v.x;
+        if (Carry<D>::NR > 1) dl[Carry<D>::NR - 1] += v.y;
+      }
       if (u.pub_slot >= 0) {
         float4 *slot = slot_ptr(qu, u.pub_slot);
-        {
+        if (!early) {
           Carry<D> S;
           S.row[0] = Td.row[0];
           S.row[Carry<D>::NR - 1] = Td.row[Carry<D>::NR - 1];
           S.tmem_load(e, tmem, L::A_Z);
           S.store_slot(e, slot);
+          Td.store_slot(e, slot + CF4 * kEpi);
         }
-        Td.store_slot(e, slot + CF4 * kEpi);
         __stcg(slot + 2 * CF4 * kEpi + e.et, make_float4(dl[0], dl[Carry<D>::NR - 1], 0.f, 0.f));
         tc_fence_before();
-        chain_publish(e, qu, u.pub_slot);
+        chain_publish(e, qu, u.pub_slot, 2);
       } else if (want_dd) {
         // <dS_T, T_T> row-wise, then the two column halves of every row meet in smem
         if (a.ds_out) {
@@ -712,6 +742,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         af[r] = chunk_alpha(a.decay, b, h, dS.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, dS.row[r], Ltail, 64);
       }
+      const bool early = u.early(qu);
+      if (early) {
+        // middle range: dS at its start follows from dS at its end and the aggregate
+        float A[Carry<D>::NR];
+        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
+        combine_store<D>(e, dS, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
+        chain_publish(e, qu, u.pub_slot);
+      }
       dS.template write_operand<BF>(e, sb + L::SB);
       fence_async_smem();
       named_bar_sync(1, kEpi);
@@ -809,8 +847,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (u.pub_slot >= 0) {
-        dS.store_slot(e, slot_ptr(qu, u.pub_slot));
-        chain_publish(e, qu, u.pub_slot);
+        if (!early) {
+          dS.store_slot(e, slot_ptr(qu, u.pub_slot));
+          chain_publish(e, qu, u.pub_slot);
+        }
       } else if (a.ds_in) {
         dS.store_rm(e, a.ds_in + sbase);
       }
@@ -842,10 +882,19 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L1::SMEM);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L2::SMEM);
   if (e != cudaSuccess) return e;
+  const int dtype = BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16;
+  if (q1.agg) {  // middle ranges: state and tangent aggregates from k, v
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q1.agg, q1.agg_f4, a.status};
+    if ((e = launch_agg_tc(1, g, a.k, a.v, q1, dtype, st)) != cudaSuccess) return e;
+  }
   k1<<<grid1, kThreads, L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (q2.agg) {  // middle ranges: dS aggregates from q and the dO the first pass wrote
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q2.agg, q2.agg_f4, a.status};
+    if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, st)) != cudaSuccess) return e;
+  }
   k2<<<grid2, kThreads, L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
   count_launches(1);
   return cudaGetLastError();

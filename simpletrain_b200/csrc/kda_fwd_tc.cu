@@ -288,6 +288,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         af[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, S.row[r], Ltail, 64);
       }
+      const bool early = u.early(qu);
+      if (early) {
+        // middle range: its exit state follows from the entry state and its aggregate
+        float A[Carry<D>::NR];
+        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
+        combine_store<D>(e, S, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
+        chain_publish(e, qu, u.pub_slot);
+      }
       S.template write_operand<BF>(e, sb + L::SB);
       fence_async_smem();
       named_bar_sync(1, kEpi);
@@ -354,9 +362,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             KDA_TRACE_EVENT(9, gc);
           }
         } else if (u.pub_slot >= 0) {
-          // hand the state across the range boundary before storing the last y
-          S.store_slot(e, slot_ptr(qu, u.pub_slot));
-          chain_publish(e, qu, u.pub_slot);
+          if (!early) {
+            // hand the state across the range boundary before storing the last y
+            S.store_slot(e, slot_ptr(qu, u.pub_slot));
+            chain_publish(e, qu, u.pub_slot);
+          }
         } else if (a.s_out) {
           S.store_rm(e, a.s_out + sbase);
         }
@@ -443,6 +453,11 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
   auto kern = fwd_tc_kernel<T, D, LIT, NS, NY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
+  if (q.agg) {  // middle ranges: their state aggregates first
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q.agg, q.agg_f4, a.status};
+    e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, st);
+    if (e != cudaSuccess) return e;
+  }
   kern<<<grid, kFwdThreads, L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
   count_launches(1);
   return cudaGetLastError();

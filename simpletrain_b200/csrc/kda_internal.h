@@ -67,11 +67,25 @@ namespace tc {
 struct Queue;
 }
 
+// Range aggregates (kda_agg_tc.cu): the carry recurrence of each middle range
+// run from zero, stored thread-major at agg + r * agg_f4 * 256 float4.
+struct AggArgs {
+  int B, H, T, D;
+  int literal;
+  DecaySrc decay;
+  float4 *agg;
+  int agg_f4;
+  int32_t *status;
+};
+
 // Launchers (return cudaError_t of the launch).  `grid` persistent CTAs work
 // through the queue's units.
 cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dtype, cudaStream_t st);
 cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue &q2, int grid1, int grid2,
                           int dtype, cudaStream_t st);
+// mode 0: S from (k, v); 1: S and decay tangent from (k, v); 2: dS from (q, dO).
+cudaError_t launch_agg_tc(int mode, const AggArgs &a, const View &va, const View &vb, const tc::Queue &q, int dtype,
+                          cudaStream_t st);
 // CTAs of the forward kernel that fit on one SM.
 int fwd_tc_occupancy(int D, int dtype, bool literal);
 

@@ -312,16 +312,25 @@ __device__ void store_frag_global(const Epi &e, const float (&val)[D / 2], const
 // ------------------------------------------------------------ scheduling --
 struct Queue {
   int *ticket;     // tickets taken so far (cleared by the host before the launch)
-  int *flags;      // [nranges + 1]: boundary slot published (cleared by the host)
+  int *flags;      // [nranges + 1]: boundary slot publish level (cleared by the host):
+                   // 1 = carried state, 2 = also the decay-gradient partial
   float4 *slots;   // [nranges + 1][slot_f4 * kEpi]: carried state at range boundary r
   int slot_f4;     // float4 per thread per slot
   int nstreams, nchunks, nranges;
+  float4 *agg;     // [nranges][agg_f4 * kEpi]: middle-range aggregates, or null
+  int agg_f4;
 };
 
 struct Piece {
   int stream, c_begin, c_end;  // chunks [c_begin, c_end) of one stream
   int wait_slot;               // boundary slot holding the entry state, or -1 (stream end / start)
   int pub_slot;                // boundary slot for the exit state, or -1
+  int range;
+  // a middle range (one piece, both ends mid-stream) with a precomputed
+  // aggregate publishes its exit state as soon as its entry state is known
+  __device__ __forceinline__ bool early(const Queue &qu) const {
+    return wait_slot >= 0 && pub_slot >= 0 && qu.agg != nullptr;
+  }
 };
 
 // Range of ticket t: stream-major positions [N t / R, N (t+1) / R), N = streams x chunks.
@@ -356,11 +365,15 @@ __device__ __forceinline__ Piece piece_of(const Queue &qu, const Span &sp, int p
   const int at_begin = pc.c_begin > 0 ? sp.r : -1, at_end = pc.c_end < qu.nchunks ? sp.r + 1 : -1;
   pc.wait_slot = reverse ? at_end : at_begin;
   pc.pub_slot = reverse ? at_begin : at_end;
+  pc.range = sp.r;
   return pc;
 }
 
 __device__ __forceinline__ float4 *slot_ptr(const Queue &qu, int slot) {
   return qu.slots + (size_t)slot * qu.slot_f4 * kEpi;
+}
+__device__ __forceinline__ const float4 *agg_ptr(const Queue &qu, int range) {
+  return qu.agg + (size_t)range * qu.agg_f4 * kEpi;
 }
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
@@ -369,16 +382,17 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   return v;
 }
 
-// Epilogue: wait until boundary `slot` has been published (one thread spins,
-// bounded), then barrier.  slot < 0: no wait.  Returns false on timeout.
+// Epilogue: wait until boundary `slot` has been published to `level` (one
+// thread spins, bounded), then barrier.  slot < 0: no wait.  Returns false on
+// timeout.
 __device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int slot, int32_t *status,
-                                           volatile int *abort_flag) {
+                                           volatile int *abort_flag, int level = 1) {
   __shared__ int ok_flag;
   if (e.et == 0) {
     int ok = 1;
-    if (slot >= 0 && ld_acquire(qu.flags + slot) == 0) {
+    if (slot >= 0 && ld_acquire(qu.flags + slot) < level) {
       const long long t0 = clock64();
-      while (ld_acquire(qu.flags + slot) == 0) {
+      while (ld_acquire(qu.flags + slot) < level) {
         if (*abort_flag || clock64() - t0 > kWaitCycles) {
           if (status) atomicOr(status, KDA_ERR_DEVICE_TIMEOUT);
           *abort_flag = 1;
@@ -397,11 +411,25 @@ __device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int sl
 // Epilogue: after every thread stored its part of the slot, publish it.  The
 // barrier orders the other threads' stores before thread 0's fence, which is
 // cumulative, so one fence suffices.
-__device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int slot) {
+__device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int slot, int level = 1) {
   named_bar_sync(1, kEpi);
   if (e.et == 0) {
     __threadfence();
-    atomicExch(qu.flags + slot, 1);
+    atomicExch(qu.flags + slot, level);
+  }
+}
+
+// Exit carry of a middle range from its entry carry x and its aggregate:
+// out = A x + agg (A = decay^(64 n) per row), stored thread-major like a slot.
+template <int D>
+__device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, const float (&A)[Carry<D>::NR],
+                                              const float4 *agg, float4 *dst) {
+  const float *f = &x.x[0][0];
+  for (int i4 = 0; i4 < Carry<D>::FLOATS / 4; ++i4) {
+    const float a = A[(4 * i4) / Carry<D>::NV];
+    const float4 g = __ldcg(agg + i4 * kEpi + e.et);
+    __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(a, f[4 * i4], g.x), fmaf(a, f[4 * i4 + 1], g.y),
+                                               fmaf(a, f[4 * i4 + 2], g.z), fmaf(a, f[4 * i4 + 3], g.w)));
   }
 }
 

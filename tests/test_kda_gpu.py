@@ -142,6 +142,31 @@ def test_backward_small(B, H, T, D, gate, dkind, with_s0, literal):
     compare(got, ref)
 
 
+# --------------------------------------------------------------------------- #
+# few streams, each much longer than a work range: the carry crosses chains of
+# middle ranges through precomputed range aggregates
+# --------------------------------------------------------------------------- #
+LONG = [
+    # B, H, T, D, gate, decay kind, s0, literal
+    (1, 1, 4096, 128, True, "channel", True, False),
+    (1, 2, 3000, 64, True, "scalar", False, False),
+    (1, 2, 2048, 64, True, "channel", True, True),
+    (2, 1, 2500, 128, False, "head", True, False),
+]
+
+
+@pytest.mark.parametrize("B,H,T,D,gate,dkind,with_s0,literal", LONG)
+def test_long_streams_forward_and_backward(B, H, T, D, gate, dkind, with_s0, literal):
+    q, k, v, g, dy, dch = _rand(B, H, T, D, gate=gate, seed=5)
+    decay = {"channel": dch, "scalar": 0.995, "head": dch[:, 0].contiguous()}[dkind]
+    s0 = torch.randn(B, H, D, D) * 0.02 if with_s0 else None
+    dsT = torch.randn(B, H, D, D) * 0.1
+    mode = "literal" if literal else "corrected"
+    ref = oracle(q, k, v, g, decay, s0, dy, dsT, mode=mode)
+    got = run_gpu(q, k, v, g, decay, s0, dy, dsT, literal=literal)
+    compare(got, ref)
+
+
 def test_fp16_inputs():
     q, k, v, g, dy, dch = _rand(1, 2, 160, 128, dtype=torch.float16, seed=2)
     ref = oracle(q, k, v, g, dch, None, dy)
