@@ -64,7 +64,7 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? KDA_OK : KDA_ERR_CUDA
 
 // ---- persistent work queue (see kda_tc_epi.cuh) ----------------------------
 // float4 per epilogue thread of one fp32 D x D carry
-int carry_f4(int D) { return (D == 128 ? 64 : 16) / 4; }
+int carry_f4(int D) { return D * D / (4 * kda::tc::kEpi); }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 

@@ -152,9 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(ok = mbar_wait(bar(ACC_FULL + buf), (k >> 1) & 1, a.status, abort_flag))) break;
       tc_fence_after();
       if (D == 128) {
-        for (int sl = 0; sl < 4; ++sl) {  // column slices of 16
+        for (int sl = 0; sl < Carry<D>::NV / 16; ++sl) {  // column slices of 16
           uint32_t u[16];
-          tmem_ld_32x32b_x16(tmem + e.lane_off + buf * D + 64 * e.half + 16 * sl, u);
+          tmem_ld_32x32b_x16(tmem + e.lane_off + buf * D + Carry<D>::W * e.cg + 16 * sl, u);
           for (int i = 0; i < 16; ++i) {
             float &sv = S.x[0][16 * sl + i];
             if (MODE == 1) Tn.x[0][16 * sl + i] = al[0] * fmaf(64.f, sv, Tn.x[0][16 * sl + i]);  // T <- a (T + L S)

@@ -397,9 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float Lf = (float)Lc;
           if (D == 128) {
             const int row = Td.row[0];
-            const uint32_t pb = sb + L::SB + (uint32_t)(e.half * L::PANEL);
-            for (int sl = 0; sl < 4; ++sl) {  // column slices of 16
-              const int col0 = 64 * e.half + 16 * sl;
+            constexpr int W = Carry<D>::W;
+            for (int sl = 0; sl < W / 16; ++sl) {  // column slices of 16
+              const int col0 = W * e.cg + 16 * sl;
+              const uint32_t pb = sb + L::SB + (uint32_t)((col0 >> 6) * L::PANEL);
               uint32_t u32[16], w32[16];
               if (c == u.c_begin) {
                 if (prev) {
@@ -430,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dl[0] += acc;
               }
               for (int j = 0; j < 2; ++j)
-                st_shared_v4(pb + swz(row, 16 * sl + 8 * j),
+                st_shared_v4(pb + swz(row, (col0 & 63) + 8 * j),
                              pack2(__uint_as_float(u32[8 * j]), __uint_as_float(u32[8 * j + 1]), BF),
                              pack2(__uint_as_float(u32[8 * j + 2]), __uint_as_float(u32[8 * j + 3]), BF),
                              pack2(__uint_as_float(u32[8 * j + 4]), __uint_as_float(u32[8 * j + 5]), BF),
@@ -481,18 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (e.et == 0) KDA_TRACE_EVENT(8, gc);
         tc_fence_after();
         if (gate) {
-          Frag<D / 2> fo;
-          ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, fo);
-          uint32_t yv[D / 8];  // all dy loads first: the shared-memory accesses are ordered asm
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee)
-              yv[2 * j + ee] = ld_shared_u32(box_addr(st + L::ST_DY, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq));
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee) {
-              const float2 y = unpack2(yv[2 * j + ee], BF);
-              st_shared_u32(box_addr(st + L::ST_DY, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
-                            pack2(y.x * fo.v(ee, j, 0), y.y * fo.v(ee, j, 1), BF));
-            }
+          frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, st + L::ST_DY, st + L::ST_DY, true);
           fence_async_smem();
           named_bar_sync(1, kEpi);
           if (e.et == 0) {
@@ -504,17 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (d) dq over the stage's gate tile (read only by the dO step), then a TMA store
         if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
         tc_fence_after();
-        {
-          Frag<D / 2> fd;
-          ld_frag(tmem + e.lane_off + A_DQ + (D / 2) * e.half, fd);
-          tc_fence_before();
-          mbar_arrive(bar(OUT_FREE));
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee) {
-              const int row = e.r0 + 8 * ee, col = (D / 2) * e.half + 8 * j + e.cq;
-              st_shared_u32(box_addr(st + L::ST_G, row, col), pack2(fd.v(ee, j, 0), fd.v(ee, j, 1), BF));
-            }
-        }
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false);
+        tc_fence_before();
+        mbar_arrive(bar(OUT_FREE));
         fence_async_smem();
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
@@ -788,9 +770,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           float al[Carry<D>::NR];
           for (int r = 0; r < Carry<D>::NR; ++r) al[r] = (Lc == 64) ? af[r] : at[r];
           if (D == 128) {
-            for (int sl = 0; sl < 2; ++sl) {
+            for (int sl = 0; sl < Carry<D>::NV / 32; ++sl) {
               uint32_t w32[32];
-              tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Z + 64 * e.half + 32 * sl, w32);
+              tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Z + Carry<D>::W * e.cg + 32 * sl, w32);
               for (int kk = 0; kk < 32; ++kk)
                 dS.x[0][32 * sl + kk] = fmaf(al[0], dS.x[0][32 * sl + kk], __uint_as_float(w32[kk]));
             }
@@ -815,25 +797,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(bar(DKV_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(24, gc);
         tc_fence_after();
-        {
-          Frag<D / 2> f;
-          ld_frag(tmem + e.lane_off + L::A_X + (D / 2) * e.half, f);
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee)
-              st_shared_u32(box_addr(sb + L::DK, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
-                            pack2(f.v(ee, j, 0), f.v(ee, j, 1), BF));
-        }
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, sb + L::DK, 0, false);
         if (e.et == 0) KDA_TRACE_EVENT(25, gc);
-        {
-          Frag<D / 2> f;
-          ld_frag(tmem + e.lane_off + L::A_Y + (D / 2) * e.half, f);
-          tc_fence_before();
-          mbar_arrive(bar(DKV_FREE));
-          for (int j = 0; j < D / 16; ++j)
-            for (int ee = 0; ee < 2; ++ee)
-              st_shared_u32(box_addr(sb + L::DV, e.r0 + 8 * ee, (D / 2) * e.half + 8 * j + e.cq),
-                            pack2(f.v(ee, j, 0), f.v(ee, j, 1), BF));
-        }
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_Y, sb + L::DV, 0, false);
+        tc_fence_before();
+        mbar_arrive(bar(DKV_FREE));
         fence_async_smem();
         named_bar_sync(1, kEpi);
         if (e.et == 0) {

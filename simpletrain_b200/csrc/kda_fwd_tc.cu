@@ -48,7 +48,7 @@ using namespace tc;
 #ifndef KDA_FWD_NY
 #define KDA_FWD_NY 4  // gate-in / y-out tiles
 #endif
-constexpr int kFwdThreads = kThreads + 32;  // + the gate-loading warp
+constexpr int kFwdThreads = kThreads;
 
 template <int D, int NS, int NY>
 struct FwdLayout {
@@ -165,6 +165,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       for (int d = gc - 1; d >= 0 && d >= gc - NS; --d)
         mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+    } else if (lane == 1) {
+      // ------------------------------------------------------- gate loader
+      if (gate) prefetch_tmap(&tg);
+      int gc = 0;
+      for (int i = 0;; ++i) {
+        if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break;
+        const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
+        mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
+        if (t >= qu.nranges) break;
+        const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
+        if (!gate) continue;
+        const int b = u.stream / a.H, h = u.stream - b * a.H;
+        bool ok = true;
+        for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
+          const int j = gc % NY, use = gc / NY;
+          if (!(ok = mbar_wait(bar(GEMPTY + j), (use & 1) ^ 1, a.status, abort_flag))) break;
+          const uint32_t yt = sb + L::Y + j * L::BOX;
+          mbar_arrive_expect_tx(bar(GFULL + j), (uint32_t)L::BOX);
+          for (int kb = 0; kb < KB; ++kb) tma_load_4d(yt + kb * kTile, &tg, bar(GFULL + j), 64 * kb, 64 * c, h, b);
+        }
+        if (!ok) break;
+      }
+      for (int d = gc - 1; d >= 0 && d >= gc - NY; --d)
+        mbar_wait(bar(GFULL + d % NY), (d / NY) & 1, a.status, abort_flag);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -233,33 +257,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       mma_commit(bar(FIN));
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
-    }
-    __syncwarp();
-  } else if (warp == 10) {
-    // ----------------------------------------------------------- gate loader
-    if (lane == 0) {
-      if (gate) prefetch_tmap(&tg);
-      int gc = 0;
-      for (int i = 0;; ++i) {
-        if (!mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, a.status, abort_flag)) break;
-        const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
-        mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
-        if (t >= qu.nranges) break;
-        const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
-        if (!gate) continue;
-        const int b = u.stream / a.H, h = u.stream - b * a.H;
-        bool ok = true;
-        for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
-          const int j = gc % NY, use = gc / NY;
-          if (!(ok = mbar_wait(bar(GEMPTY + j), (use & 1) ^ 1, a.status, abort_flag))) break;
-          const uint32_t yt = sb + L::Y + j * L::BOX;
-          mbar_arrive_expect_tx(bar(GFULL + j), (uint32_t)L::BOX);
-          for (int kb = 0; kb < KB; ++kb) tma_load_4d(yt + kb * kTile, &tg, bar(GFULL + j), 64 * kb, 64 * c, h, b);
-        }
-        if (!ok) break;
-      }
-      for (int d = gc - 1; d >= 0 && d >= gc - NY; --d)
-        mbar_wait(bar(GFULL + d % NY), (d / NY) & 1, a.status, abort_flag);
     }
     __syncwarp();
   } else {
@@ -332,11 +329,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const bool upd = !(LIT && Lc != 64);
           if (D == 128) {
             const float al = (Lc == 64) ? af[0] : at[0];
-            for (int sl = 0; sl < 2; ++sl) {
+            for (int sl = 0; sl < Carry<D>::NV / 32; ++sl) {
               uint32_t uu[32];
-              tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_KV + 64 * e.half + 32 * sl, uu);
+              tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_KV + Carry<D>::W * e.cg + 32 * sl, uu);
               if (upd)
-                for (int k = 0; k < 32; ++k) S.x[0][32 * sl + k] = fmaf(al, S.x[0][32 * sl + k], __uint_as_float(uu[k]));
+                for (int k = 0; k < 32; ++k)
+                  S.x[0][32 * sl + k] = fmaf(al, S.x[0][32 * sl + k], __uint_as_float(uu[k]));
             }
           } else {
             Carry<D> U;
@@ -379,8 +377,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (e.et == 0) KDA_TRACE_EVENT(10, gc);
         tc_fence_after();
         {
-          Frag<D / 2> fo;
-          ld_frag(tmem + e.lane_off + (ob ? L::A_O1 : L::A_O0) + (D / 2) * e.half, fo);
+          constexpr int W = D / kQ;
+          Frag<W> fo;
+          ld_frag(tmem + e.lane_off + (ob ? L::A_O1 : L::A_O0) + W * e.cg, fo);
           tc_fence_before();
           mbar_arrive(bar(O_FREE0 + ob));
           if (e.et == 0) KDA_TRACE_EVENT(20, gc);
@@ -390,12 +389,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             named_bar_sync(1, kEpi);
           }
           if (e.et == 0) KDA_TRACE_EVENT(21, gc);
-          uint32_t gv[D / 8];  // all gate loads first: the shared-memory accesses are ordered asm
+          uint32_t gv[W / 4];  // all gate loads first: the shared-memory accesses are ordered asm
           if (gate)
-            for (int jj = 0; jj < D / 16; ++jj)
+            for (int jj = 0; jj < W / 8; ++jj)
               for (int ee = 0; ee < 2; ++ee)
-                gv[2 * jj + ee] = ld_shared_u32(box_addr(yt, e.r0 + 8 * ee, (D / 2) * e.half + 8 * jj + e.cq));
-          for (int jj = 0; jj < D / 16; ++jj)
+                gv[2 * jj + ee] = ld_shared_u32(box_addr(yt, e.r0 + 8 * ee, W * e.cg + 8 * jj + e.cq));
+          for (int jj = 0; jj < W / 8; ++jj)
             for (int ee = 0; ee < 2; ++ee) {
               float o0 = fo.v(ee, jj, 0), o1 = fo.v(ee, jj, 1);
               if (gate) {
@@ -404,7 +403,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 o1 *= g2.y;
               }
               // y over g, element by element
-              st_shared_u32(box_addr(yt, e.r0 + 8 * ee, (D / 2) * e.half + 8 * jj + e.cq), pack2(o0, o1, BF));
+              st_shared_u32(box_addr(yt, e.r0 + 8 * ee, W * e.cg + 8 * jj + e.cq), pack2(o0, o1, BF));
             }
           if (e.et == 0) KDA_TRACE_EVENT(22, gc);
           fence_async_smem();

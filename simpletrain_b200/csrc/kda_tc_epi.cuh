@@ -65,32 +65,35 @@ namespace kda {
 namespace tc {
 
 constexpr int kTile = 64 * 64 * 2;  // one [64 x 64] 16-bit box, 8 KB
-constexpr int kEpi = 256;           // epilogue threads (warps 2..9)
-constexpr int kThreads = 320;       // + TMA warp + MMA warp
+constexpr int kQ = 2;               // epilogue warps per TMEM sub-partition: column groups
+constexpr int kEpi = 128 * kQ;      // epilogue threads (warps 2 .. 1 + 4 kQ)
+constexpr int kThreads = 64 + kEpi; // + TMA warp + MMA warp
 
 // ------------------------------------------------------------- geometry --
-// Two epilogue warps per TMEM sub-partition: `half` splits the columns.
+// kQ epilogue warps per TMEM sub-partition (TMEM lanes 32 sp .. 32 sp + 31);
+// column group `cg` owns 1 / kQ of every accumulator's columns.
 struct Epi {
-  int et, lane, sp, half, r0, cq;
+  int et, lane, sp, cg, r0, cq;
   uint32_t lane_off;
   __device__ Epi() {
     et = threadIdx.x - 64;
     lane = threadIdx.x & 31;
     sp = (threadIdx.x >> 5) & 3;
-    half = et >> 7;
+    cg = et >> 7;
     r0 = 16 * sp + (lane >> 2);
     cq = 2 * (lane & 3);
     lane_off = (uint32_t)(32 * sp) << 16;
   }
 };
 
-// M=64 accumulator fragment, W columns per half: rows r0 and r0+8,
-// columns col0 + 8j + cq + {0,1}; value (e, j, k) at r[4j + 2e + k].
+// M=64 accumulator fragment of W columns per warp: rows r0 and r0+8,
+// columns W*cg + 8j + cq + {0,1}; value (e, j, k) at r[4j + 2e + k].
 template <int W>
 struct Frag {
   uint32_t r[W / 2];
   __device__ __forceinline__ float v(int e, int j, int k) const { return __uint_as_float(r[4 * j + 2 * e + k]); }
 };
+__device__ __forceinline__ void ld_frag(uint32_t taddr, Frag<16> &f) { tmem_ld_16x256b_x2(taddr, f.r); }
 __device__ __forceinline__ void ld_frag(uint32_t taddr, Frag<32> &f) { tmem_ld_16x256b_x4(taddr, f.r); }
 __device__ __forceinline__ void ld_frag(uint32_t taddr, Frag<64> &f) { tmem_ld_16x256b_x8(taddr, f.r); }
 
@@ -105,18 +108,20 @@ __device__ __forceinline__ uint32_t panel_addr(uint32_t base, int row, int col) 
 }
 
 // ------------------------------------------------------------------ carry --
-// fp32 D x D carry (state or its gradient / tangent) owned by the epilogue:
-//   D=128 (M=128 accumulators): row 32*sp + lane, columns 64*half + [0, 64)
-//   D=64  (M=64 accumulators) : rows r0, r0+8, columns 32*half + 8j + cq + k (j < 4)
+// fp32 D x D carry (state or its gradient / tangent) owned by the epilogue,
+// W = D / kQ columns per thread group:
+//   D=128 (M=128 accumulators): row 32*sp + lane, columns W*cg + [0, W)
+//   D=64  (M=64 accumulators) : rows r0, r0+8, columns W*cg + 8j + cq + k (j < W/8)
 template <int D>
 struct Carry {
+  static constexpr int W = D / kQ;
   static constexpr int NR = (D == 128) ? 1 : 2;
-  static constexpr int NV = (D == 128) ? 64 : 8;
+  static constexpr int NV = (D == 128) ? W : W / 4;
   static constexpr int FLOATS = NR * NV;  // per thread
   float x[NR][NV];
   int row[NR];
   __device__ __forceinline__ int col(const Epi &e, int i) const {
-    return (D == 128) ? 64 * e.half + i : 32 * e.half + 8 * (i >> 1) + e.cq + (i & 1);
+    return (D == 128) ? W * e.cg + i : W * e.cg + 8 * (i >> 1) + e.cq + (i & 1);
   }
   __device__ void init_rows(const Epi &e) {
     if (D == 128) row[0] = 32 * e.sp + e.lane;
@@ -133,9 +138,9 @@ struct Carry {
       zero();
       return;
     }
-    if (D == 128) {
-      const float4 *s4 = reinterpret_cast<const float4 *>(src + (size_t)row[0] * D + 64 * e.half);
-      for (int i = 0; i < 16; ++i) {
+    if constexpr (D == 128) {
+      const float4 *s4 = reinterpret_cast<const float4 *>(src + (size_t)row[0] * D + W * e.cg);
+      for (int i = 0; i < NV / 4; ++i) {
         const float4 v = __ldg(s4 + i);
         x[0][4 * i] = v.x; x[0][4 * i + 1] = v.y; x[0][4 * i + 2] = v.z; x[0][4 * i + 3] = v.w;
       }
@@ -149,9 +154,10 @@ struct Carry {
     }
   }
   __device__ void store_rm(const Epi &e, float *dst) const {
-    if (D == 128) {
-      float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)row[0] * D + 64 * e.half);
-      for (int i = 0; i < 16; ++i) d4[i] = make_float4(x[0][4 * i], x[0][4 * i + 1], x[0][4 * i + 2], x[0][4 * i + 3]);
+    if constexpr (D == 128) {
+      float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)row[0] * D + W * e.cg);
+      for (int i = 0; i < NV / 4; ++i)
+        d4[i] = make_float4(x[0][4 * i], x[0][4 * i + 1], x[0][4 * i + 2], x[0][4 * i + 3]);
     } else {
       for (int r = 0; r < NR; ++r)
         for (int j = 0; j < NV / 2; ++j)
@@ -173,63 +179,64 @@ struct Carry {
   }
   // tensor memory (M = D accumulator at column base `acc`)
   __device__ void tmem_load(const Epi &e, uint32_t tmem, uint32_t acc) {
-    if (D == 128) {
-      uint32_t u[32];
-      tmem_ld_32x32b_x32(tmem + e.lane_off + acc + 64 * e.half, u);
-      for (int i = 0; i < 32; ++i) x[0][i] = __uint_as_float(u[i]);
-      tmem_ld_32x32b_x32(tmem + e.lane_off + acc + 64 * e.half + 32, u);
-      for (int i = 0; i < 32; ++i) x[0][32 + i] = __uint_as_float(u[i]);
+    if constexpr (D == 128) {
+      for (int sl = 0; sl < W / 32; ++sl) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tmem + e.lane_off + acc + W * e.cg + 32 * sl, u);
+        for (int i = 0; i < 32; ++i) x[0][32 * sl + i] = __uint_as_float(u[i]);
+      }
     } else {
-      Frag<32> f;
-      ld_frag(tmem + e.lane_off + acc + 32 * e.half, f);
+      Frag<W> f;
+      ld_frag(tmem + e.lane_off + acc + W * e.cg, f);
       for (int r = 0; r < NR; ++r)
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < W / 8; ++j)
           for (int k = 0; k < 2; ++k) x[r][2 * j + k] = f.v(r, j, k);
     }
   }
   __device__ void tmem_store(const Epi &e, uint32_t tmem, uint32_t acc) const {
-    if (D == 128) {
-      uint32_t u[32];
-      for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(x[0][i]);
-      tmem_st_32x32b_x32(tmem + e.lane_off + acc + 64 * e.half, u);
-      for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(x[0][32 + i]);
-      tmem_st_32x32b_x32(tmem + e.lane_off + acc + 64 * e.half + 32, u);
+    if constexpr (D == 128) {
+      for (int sl = 0; sl < W / 32; ++sl) {
+        uint32_t u[32];
+        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(x[0][32 * sl + i]);
+        tmem_st_32x32b_x32(tmem + e.lane_off + acc + W * e.cg + 32 * sl, u);
+      }
     } else {
-      uint32_t u[16];
+      uint32_t u[W / 2];
       for (int r = 0; r < NR; ++r)
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < W / 8; ++j)
           for (int k = 0; k < 2; ++k) u[4 * j + 2 * r + k] = __float_as_uint(x[r][2 * j + k]);
-      tmem_st_16x256b_x4(tmem + e.lane_off + acc + 32 * e.half, u);
+      if constexpr (W == 16) tmem_st_16x256b_x2(tmem + e.lane_off + acc + W * e.cg, u);
+      else tmem_st_16x256b_x4(tmem + e.lane_off + acc + W * e.cg, u);
     }
   }
   // 16-bit copy into a state operand (panels of [D rows x 64 cols])
   template <bool BF>
   __device__ void write_operand(const Epi &e, uint32_t base) const {
-    if (D == 128) {
-      const uint32_t pb = base + (uint32_t)(e.half * D * 128);
-      for (int j = 0; j < 8; ++j)
-        st_shared_v4(pb + swz(row[0], 8 * j), pack2(x[0][8 * j], x[0][8 * j + 1], BF),
+    if constexpr (D == 128) {
+      for (int j = 0; j < W / 8; ++j)
+        st_shared_v4(panel_addr<D>(base, row[0], W * e.cg + 8 * j), pack2(x[0][8 * j], x[0][8 * j + 1], BF),
                      pack2(x[0][8 * j + 2], x[0][8 * j + 3], BF), pack2(x[0][8 * j + 4], x[0][8 * j + 5], BF),
                      pack2(x[0][8 * j + 6], x[0][8 * j + 7], BF));
     } else {
       for (int r = 0; r < NR; ++r)
-        for (int j = 0; j < 4; ++j)
-          st_shared_u32(panel_addr<D>(base, row[r], 32 * e.half + 8 * j + e.cq),
-                        pack2(x[r][2 * j], x[r][2 * j + 1], BF));
+        for (int j = 0; j < W / 8; ++j)
+          st_shared_u32(panel_addr<D>(base, row[r], W * e.cg + 8 * j + e.cq), pack2(x[r][2 * j], x[r][2 * j + 1], BF));
     }
   }
 };
+static_assert(kQ == 2 || kQ == 4, "column groups of 64 or 32 (D=128) and 32 or 16 (D=64)");
 
 // ---------------------------------------------------------- tile helpers --
-// dO = dy * g (or dy) into the DO tile; all 256 epilogue threads.
+// dO = dy * g (or dy) into the DO tile; all epilogue threads, eight per row.
 template <int D, bool BF>
 __device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_t do_tile, bool gate) {
-  constexpr int N = 2 * (D / 64);  // 16-byte chunks per thread
-  const int row = e.et >> 2, q4 = e.et & 3;
+  constexpr int TPR = kEpi / 64;            // threads per row
+  constexpr int N = 8 * (D / 64) / TPR;    // 16-byte chunks per thread
+  const int row = e.et / TPR, q = e.et % TPR;
   uint32_t off[N];
   uint4 y[N], g[N];
   for (int i = 0; i < N; ++i) {  // all loads first: the shared-memory accesses are ordered asm
-    const int ch = q4 + 4 * i;
+    const int ch = q + TPR * i;
     off[i] = (uint32_t)((ch >> 3) * kTile) + (uint32_t)(row * 128) + ((((ch & 7) ^ (row & 7)) & 7) << 4);
     y[i] = ld_shared_v4(dy_tile + off[i]);
     if (gate) g[i] = ld_shared_v4(g_tile + off[i]);
@@ -247,15 +254,17 @@ __device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_
   }
 }
 
-// Masked (col <= row) M=64, N=64 accumulator -> 16-bit [64 x 64] tile; each half owns 32 columns.
-// Ends with tcgen05.fence::before_thread_sync (the accumulator may be reused after a barrier).
+// Masked (col <= row) M=64, N=64 accumulator -> 16-bit [64 x 64] tile; each
+// column group owns 64 / kQ columns.  Ends with tcgen05.fence::before_thread_sync
+// (the accumulator may be reused after a barrier).
 template <bool BF>
 __device__ void masked_tile(const Epi &e, uint32_t taddr, uint32_t dst) {
-  Frag<32> f;
-  ld_frag(taddr + 32 * e.half, f);
+  constexpr int W = 64 / kQ;
+  Frag<W> f;
+  ld_frag(taddr + W * e.cg, f);
   tc_fence_before();
-  for (int j = 0; j < 4; ++j) {
-    const int col = 32 * e.half + 8 * j + e.cq;
+  for (int j = 0; j < W / 8; ++j) {
+    const int col = W * e.cg + 8 * j + e.cq;
     for (int ee = 0; ee < 2; ++ee) {
       const int row = e.r0 + 8 * ee;
       const float a0 = col <= row ? f.v(ee, j, 0) : 0.f;
@@ -265,48 +274,30 @@ __device__ void masked_tile(const Epi &e, uint32_t taddr, uint32_t dst) {
   }
 }
 
-// Store an M=64 fragment of W = D/2 fp32 values per thread (rows r0, r0+8 of a
-// 64-token chunk; columns (D/2)*half + 8j + cq + k) to global memory as 16-bit
-// values.  A 4x4 transpose inside each lane quad gives every thread whole
-// 16-byte groups of 8 columns.  Rows >= L (ragged last chunk) are skipped.
+// M=64 accumulator of D columns at `taddr` -> 16-bit tile at `tile` (KB boxes),
+// each value optionally scaled by the 16-bit tile `scale` at the same place
+// (which may be `tile` itself).  Loads go first: the shared-memory accesses are
+// ordered asm.
 template <int D, bool BF>
-__device__ void store_frag_global(const Epi &e, const float (&val)[D / 2], const View &v, int b, int h, int t0,
-                                  int L) {
-  constexpr int NJ = D / 16;  // 8-column groups per half
-  const int q = e.lane & 3;
-  uint32_t p[2][NJ];          // packed pairs: row sel, group j
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    p[0][j] = pack2(val[4 * j], val[4 * j + 1], BF);
-    p[1][j] = pack2(val[4 * j + 2], val[4 * j + 3], BF);
-  }
-#pragma unroll
-  for (int ee = 0; ee < 2; ++ee) {
-    const int row = e.r0 + 8 * ee;
-#pragma unroll
-    for (int m = 0; m < NJ / 4; ++m) {
-      // after the exchange, w[k] = pair k (columns 2k, 2k+1) of group 4m+q;
-      // every index below is a compile-time constant (no local memory)
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int sel = (q - r) & 3;
-        uint32_t sv = p[ee][4 * m];
-#pragma unroll
-        for (int jj = 1; jj < 4; ++jj) sv = (sel == jj) ? p[ee][4 * m + jj] : sv;
-        const uint32_t got = __shfl_sync(0xffffffffu, sv, (e.lane & ~3) | ((q + r) & 3));
-        const int dst = (q + r) & 3;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) w[k] = (dst == k) ? got : w[k];
+__device__ __forceinline__ void frag_to_tile(const Epi &e, uint32_t taddr, uint32_t tile, uint32_t scale,
+                                             bool scaled) {
+  constexpr int W = D / kQ;
+  Frag<W> f;
+  ld_frag(taddr + W * e.cg, f);
+  uint32_t sv[W / 4];
+  if (scaled)
+    for (int j = 0; j < W / 8; ++j)
+      for (int ee = 0; ee < 2; ++ee) sv[2 * j + ee] = ld_shared_u32(box_addr(scale, e.r0 + 8 * ee, W * e.cg + 8 * j + e.cq));
+  for (int j = 0; j < W / 8; ++j)
+    for (int ee = 0; ee < 2; ++ee) {
+      float v0 = f.v(ee, j, 0), v1 = f.v(ee, j, 1);
+      if (scaled) {
+        const float2 s2 = unpack2(sv[2 * j + ee], BF);
+        v0 *= s2.x;
+        v1 *= s2.y;
       }
-      if (row < L) {
-        const int col = (D / 2) * e.half + 8 * (4 * m + q);
-        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(v.data) + b * v.sb + h * v.sh +
-                                               (int64_t)(t0 + row) * v.st + col);
-        *dst = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+      st_shared_u32(box_addr(tile, e.r0 + 8 * ee, W * e.cg + 8 * j + e.cq), pack2(v0, v1, BF));
     }
-  }
 }
 
 // ------------------------------------------------------------ scheduling --
