@@ -141,7 +141,7 @@ def traffic_from_profiles(w, kernel: str):
 def run_ours(args, w, rank, world, local_rank):
     import torch.distributed as dist
 
-    import simpletrain_b200  # noqa: F401  (registers the ops)
+    import simpletrain_b200.ops  # noqa: F401  (loads the ops)
     from simpletrain_b200 import _ffi
     from simpletrain_b200.ops import device_status, kda_chunk
 

@@ -1,6 +1,6 @@
 """CPU oracle for SimpleTrain's KDA chunked scan -- TEST INFRASTRUCTURE ONLY.
 
-This module is the checker, never the product: only ``tests/``,
+This module is test infrastructure, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference``
 legs of ``bench.py`` may import it.  The CUDA product path never calls it.
 

@@ -12,7 +12,16 @@ output_final_state) -> (y, final_state)``
 ``device_status()``
     read device-side error bits (bounded waits that expired).
 """
-from .ops import device_status, kda_chunk  # noqa: F401
-from .kda_kernel import install, kda_chunked_scan  # noqa: F401
-
 __all__ = ["kda_chunk", "kda_chunked_scan", "install", "device_status"]
+
+
+def __getattr__(name):
+    # loaded on first use, so that building (``python -m simpletrain_b200.build``)
+    # does not need the built libraries
+    if name in ("kda_chunk", "device_status"):
+        from . import ops
+        return getattr(ops, name)
+    if name in ("install", "kda_chunked_scan"):
+        from . import kda_kernel
+        return getattr(kda_kernel, name)
+    raise AttributeError(f"module 'simpletrain_b200' has no attribute {name!r}")

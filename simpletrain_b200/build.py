@@ -1,9 +1,10 @@
-"""Build the sm_100a KDA library in-tree: ``simpletrain_b200/_lib/libkda_sm100.so``.
+"""Build the sm_100a KDA library in-tree: ``simpletrain_b200/_lib/libkda_sm100.so``
+(plain nvcc, one shared object exporting the C ABI of ``include/kda_sm100.h``)
+and the torch ops over it, ``simpletrain_b200/_lib/kda_b200_ops.so``.
 
     python -m simpletrain_b200.build            # build if sources changed
     python -m simpletrain_b200.build --force    # rebuild
 
-Plain nvcc, one shared object exporting the C ABI of ``include/kda_sm100.h``.
 Cross-compiles without a GPU.
 """
 from __future__ import annotations
@@ -37,6 +38,47 @@ def nvcc_path() -> str:
 
 def sources():
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+TORCH_OPS = os.path.join(LIBDIR, "kda_b200_ops.so")
+TORCH_OPS_SRC = os.path.join(CSRC, "torch_ops.cpp")
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Build the torch dispatcher ops (``csrc/torch_ops.cpp``) against the C ABI
+    library into ``_lib/kda_b200_ops.so`` (in-tree, loaded by ``simpletrain_b200.ops``)."""
+    import torch
+
+    h = hashlib.sha256()
+    for f in (TORCH_OPS_SRC, os.path.join(ROOT, "include", "kda_sm100.h")):
+        with open(f, "rb") as fh:
+            h.update(fh.read())
+    h.update(torch.__version__.encode())
+    digest = h.hexdigest()
+    stamp = TORCH_OPS + ".srchash"
+    if not force and os.path.exists(TORCH_OPS) and os.path.exists(stamp):
+        with open(stamp) as fh:
+            if fh.read().strip() == digest:
+                return TORCH_OPS
+    bdir = os.path.join(LIBDIR, "_torch_build")
+    os.makedirs(bdir, exist_ok=True)
+    # compile in a child process: torch's loader registers the ops in the
+    # process that builds them, and they may be registered only once per process
+    code = (
+        "from torch.utils.cpp_extension import load\n"
+        f"load(name='kda_b200_ops', sources=[{TORCH_OPS_SRC!r}], build_directory={bdir!r}, with_cuda=True,\n"
+        f"     extra_cflags=['-O2'], extra_include_paths=[{os.path.join(ROOT, 'include')!r}],\n"
+        # $ORIGIN escaped for ninja ($$) and the shell (\\): the C ABI library sits beside this one
+        f"     extra_ldflags=['-L{LIBDIR}', '-lkda_sm100', '-Wl,-rpath,\\\\$$ORIGIN:\\\\$$ORIGIN/..'],\n"
+        f"     is_python_module=False, verbose={bool(verbose)})\n")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("torch ops build failed:\n" + res.stdout + res.stderr)
+    shutil.copyfile(os.path.join(bdir, "kda_b200_ops.so"), TORCH_OPS + ".tmp")
+    os.replace(TORCH_OPS + ".tmp", TORCH_OPS)
+    with open(stamp, "w") as fh:
+        fh.write(digest)
+    return TORCH_OPS
 
 
 def _hash() -> str:
@@ -87,6 +129,8 @@ def main(argv=None):
     ap.add_argument("--trace", action="store_true", help="build the tracing development variant")
     args = ap.parse_args(argv)
     print(build(force=args.force, verbose=args.verbose, trace=args.trace))
+    if not args.trace:
+        print(build_torch_ops(force=args.force, verbose=args.verbose))
 
 
 if __name__ == "__main__":

@@ -1,25 +1,33 @@
-"""torch.library custom ops over the sm_100a KDA C ABI, with autograd.
+"""torch ops over the sm_100a KDA C ABI, with autograd.
 
-``kda_b200::chunk_fwd`` and ``kda_b200::chunk_bwd`` call ``kda_fwd_sm100`` /
-``kda_bwd_sm100`` (``include/kda_sm100.h``) on torch's current CUDA stream,
-with outputs and workspace from the caching allocator, so they can be captured
-in CUDA graphs and traced by ``torch.compile`` (fake implementations are
-registered).  A nonzero ABI status raises ``RuntimeError``.  There is no CPU
-or fallback path: CPU tensors are rejected.
+``kda_b200::chunk_fwd`` and ``kda_b200::chunk_bwd`` are defined and
+implemented in C++ (``csrc/torch_ops.cpp``, built into
+``_lib/kda_b200_ops.so``): they call ``kda_fwd_sm100`` / ``kda_bwd_sm100``
+(``include/kda_sm100.h``) on torch's current CUDA stream, with outputs and
+workspace from the caching allocator, so they can be captured in CUDA graphs.
+This module loads them and registers their fake implementations (for
+``torch.compile`` tracing) and the autograd formula.  A nonzero ABI status
+raises ``RuntimeError``.  There is no CPU or fallback path: CPU tensors are
+rejected, and a missing build raises ``ImportError``.
 """
 from __future__ import annotations
 
-import ctypes
-from typing import Dict, Optional, Tuple, Union
+import os
+from typing import Optional, Tuple, Union
 
 import torch
 
 from . import _ffi
+from .build import TORCH_OPS
 
 Tensor = torch.Tensor
 
 _DTYPES = {torch.bfloat16: _ffi.KDA_DTYPE_BF16, torch.float16: _ffi.KDA_DTYPE_F16}
-_STATUS: Dict[int, Tensor] = {}
+
+if not os.path.exists(TORCH_OPS):
+    raise ImportError(f"KDA torch ops not built ({TORCH_OPS}); run `python -m simpletrain_b200.build`")
+_ffi.load()                       # the C ABI library (status strings, diagnostics)
+torch.ops.load_library(TORCH_OPS)  # defines kda_b200::chunk_fwd / chunk_bwd / status_word
 
 
 def _lib():
@@ -29,11 +37,7 @@ def _lib():
 def status_word(device: torch.device) -> Tensor:
     """Per-device int32 word the kernels OR device-side error bits into."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    w = _STATUS.get(idx)
-    if w is None:
-        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-        _STATUS[idx] = w
-    return w
+    return torch.ops.kda_b200.status_word(idx)
 
 
 def device_status(device: Union[torch.device, int, None] = None, reset: bool = True) -> int:
@@ -82,11 +86,6 @@ def _decay_fields(decay: Optional[Tensor]):
     return decay.data_ptr(), st[0], st[1], st[2]
 
 
-def _check(rc: int, what: str):
-    if rc != _ffi.KDA_OK:
-        raise RuntimeError(f"{what} failed: {_ffi.status_string(rc)} (status {rc})")
-
-
 def _validate(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], chunk: int):
     if q.device.type != "cuda":
         raise RuntimeError("the KDA sm_100a kernels need CUDA tensors (there is no CPU path)")
@@ -104,84 +103,16 @@ def _validate(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], chunk: int):
 
 
 # --------------------------------------------------------------------------- #
-# forward op
+# fake implementations (shapes only) for tracing
 # --------------------------------------------------------------------------- #
-@torch.library.custom_op("kda_b200::chunk_fwd", mutates_args=())
-def chunk_fwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], decay: Optional[Tensor],
-              decay_scalar: float, s0: Optional[Tensor], chunk: int, literal: bool,
-              want_state: bool) -> Tuple[Tensor, Tensor]:
-    q, k, v, g = _prep(q), _prep(k), _prep(v), _prep(g)
-    B, H, T, D = q.shape
-    y = torch.empty_like(q)               # like the reference (:263): keeps q's memory order
-    y = _prep(y)
-    s_out = (torch.empty(B, H, D, D, dtype=torch.float32, device=q.device) if want_state
-             else torch.empty(0, dtype=torch.float32, device=q.device))
-    s_in = s0.contiguous().float() if s0 is not None else None
-    lib = _lib()
-    flags = _ffi.KDA_FLAG_LITERAL if literal else 0
-    ws_bytes = lib.kda_fwd_workspace_bytes(B, H, T, D, chunk, flags)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-    dptr, dsb, dsh, dsd = _decay_fields(decay)
-    p = _ffi.KdaFwdParams(
-        B, H, T, D, chunk, _DTYPES[q.dtype], flags,
-        _desc(q), _desc(k), _desc(v), _desc(g), _desc(y),
-        dptr, dsb, dsh, dsd, float(decay_scalar),
-        _ptr(s_in), _ptr(s_out) if want_state else None,
-        _ptr(ws), ws_bytes, status_word(q.device).data_ptr(),
-    )
-    rc = lib.kda_fwd_sm100(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream))
-    _check(rc, "kda_fwd_sm100")
-    return y, s_out
-
-
-@chunk_fwd.register_fake
+@torch.library.register_fake("kda_b200::chunk_fwd")
 def _(q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state):
     B, H, T, D = q.shape
     shape = (B, H, D, D) if want_state else (0,)
     return torch.empty_like(q), q.new_empty(shape, dtype=torch.float32)
 
 
-# --------------------------------------------------------------------------- #
-# backward op
-# --------------------------------------------------------------------------- #
-@torch.library.custom_op("kda_b200::chunk_bwd", mutates_args=())
-def chunk_bwd(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], dy: Tensor,
-              decay: Optional[Tensor], decay_scalar: float, s0: Optional[Tensor],
-              s_T: Optional[Tensor], ds_T: Optional[Tensor], chunk: int, literal: bool,
-              need_ddecay: bool, need_ds0: bool
-              ) -> Tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
-    q, k, v, g, dy = _prep(q), _prep(k), _prep(v), _prep(g), _prep(dy)
-    B, H, T, D = q.shape
-    dev = q.device
-    dq, dk, dv = _prep(torch.empty_like(q)), _prep(torch.empty_like(k)), _prep(torch.empty_like(v))
-    dg = _prep(torch.empty_like(g)) if g is not None else torch.empty(0, dtype=q.dtype, device=dev)
-    need_ddecay = bool(need_ddecay and decay is not None)
-    ddecay = (torch.empty(B, H, D, dtype=torch.float32, device=dev) if need_ddecay
-              else torch.empty(0, dtype=torch.float32, device=dev))
-    ds0 = (torch.empty(B, H, D, D, dtype=torch.float32, device=dev) if need_ds0
-           else torch.empty(0, dtype=torch.float32, device=dev))
-    s_in = s0.contiguous().float() if s0 is not None else None
-    dsT = ds_T.contiguous().float() if (ds_T is not None and ds_T.numel()) else None
-    lib = _lib()
-    flags = _ffi.KDA_FLAG_LITERAL if literal else 0
-    ws_bytes = lib.kda_bwd_workspace_bytes(B, H, T, D, chunk, flags)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
-    dptr, dsb, dsh, dsd = _decay_fields(decay)
-    p = _ffi.KdaBwdParams(
-        B, H, T, D, chunk, _DTYPES[q.dtype], flags,
-        _desc(q), _desc(k), _desc(v), _desc(g), _desc(dy),
-        _desc(dq), _desc(dk), _desc(dv), _desc(dg if g is not None else None),
-        dptr, dsb, dsh, dsd, float(decay_scalar),
-        _ptr(s_in), _ptr(dsT),
-        _ptr(ds0) if need_ds0 else None, _ptr(ddecay) if need_ddecay else None,
-        _ptr(ws), ws_bytes, status_word(dev).data_ptr(),
-    )
-    rc = lib.kda_bwd_sm100(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
-    _check(rc, "kda_bwd_sm100")
-    return dq, dk, dv, dg, ddecay, ds0
-
-
-@chunk_bwd.register_fake
+@torch.library.register_fake("kda_b200::chunk_bwd")
 def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, literal, need_ddecay, need_ds0):
     B, H, T, D = q.shape
     f32 = torch.float32
@@ -191,6 +122,9 @@ def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, literal, need_d
     return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), dg, dd, ds0
 
 
+# --------------------------------------------------------------------------- #
+# autograd
+# --------------------------------------------------------------------------- #
 def _setup_context(ctx, inputs, output):
     q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state = inputs
     y, s_T = output
