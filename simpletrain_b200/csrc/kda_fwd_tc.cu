@@ -464,10 +464,16 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
 
 template <typename T, int D, bool LIT, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
 int fwd_ctas_per_sm() {
+  auto kern = fwd_tc_kernel<T, D, LIT, NS, NY>;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fwd_tc_kernel<T, D, LIT, NS, NY>, kFwdThreads,
-                                                    FwdLayout<D, NS, NY>::SMEM) != cudaSuccess)
+  // the dynamic shared memory must be allowed before the occupancy query counts it
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<D, NS, NY>::SMEM) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kFwdThreads, FwdLayout<D, NS, NY>::SMEM) != cudaSuccess)
     return 1;
+  // tensor memory is not in the occupancy model: a CTA holds TMEM_COLS of the SM's 512 columns
+  const int tmem_cap = 512 / (int)FwdLayout<D, NS, NY>::TMEM_COLS;
+  n = n < tmem_cap ? n : tmem_cap;
   return n > 0 ? n : 1;
 }
 

@@ -18,7 +18,8 @@ from typing import Optional, Tuple, Union
 import torch
 
 from . import _ffi
-from .build import TORCH_OPS
+
+TORCH_OPS = os.path.join(_ffi.LIB_DIR, "kda_b200_ops.so")
 
 Tensor = torch.Tensor
 
