@@ -31,6 +31,9 @@ KDA_ERR_DEVICE_TIMEOUT = 64
 EXPORTED = (
     "kda_fwd_sm100", "kda_bwd_sm100", "kda_fwd_workspace_bytes", "kda_bwd_workspace_bytes",
     "kda_status_string", "kda_abi_version", "kda_launch_count", "kda_fwd_sm100_noalloc",
+    # include/st_fused_ops.h
+    "st_silu_mul_fwd", "st_silu_mul_bwd", "st_rmsnorm_residual_fwd", "st_rmsnorm_residual_bwd",
+    "st_rmsnorm_residual_bwd_scratch", "st_cross_entropy_fwd", "st_cross_entropy_bwd",
 )
 NOALLOC_SCRATCH_BYTES = 32 << 20
 

@@ -50,7 +50,7 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
     import torch
 
     h = hashlib.sha256()
-    for f in (TORCH_OPS_SRC, os.path.join(ROOT, "include", "kda_sm100.h")):
+    for f in (TORCH_OPS_SRC, os.path.join(ROOT, "include", "kda_sm100.h"), os.path.join(ROOT, "include", "st_fused_ops.h")):
         with open(f, "rb") as fh:
             h.update(fh.read())
     h.update(torch.__version__.encode())

@@ -1,6 +1,9 @@
-// torch dispatcher ops over the C ABI of include/kda_sm100.h:
-//   kda_b200::chunk_fwd  -> kda_fwd_sm100
-//   kda_b200::chunk_bwd  -> kda_bwd_sm100
+// torch dispatcher ops over the C ABIs of include/kda_sm100.h and
+// include/st_fused_ops.h:
+//   kda_b200::chunk_fwd / chunk_bwd            -> kda_fwd_sm100 / kda_bwd_sm100
+//   st_b200::silu_mul / silu_mul_bwd           -> st_silu_mul_fwd / _bwd
+//   st_b200::rmsnorm_residual / _bwd           -> st_rmsnorm_residual_fwd / _bwd
+//   st_b200::cross_entropy / cross_entropy_bwd -> st_cross_entropy_fwd / _bwd
 //
 // The schemas and CUDA implementations live here, in C++, so a call costs a
 // dispatcher hop and a few caching-allocator allocations instead of a Python
@@ -21,6 +24,7 @@
 #include <vector>
 
 #include "../../include/kda_sm100.h"
+#include "../../include/st_fused_ops.h"
 
 namespace {
 
@@ -182,7 +186,110 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> chunk_bwd(
 // The status word the kernels write (Python reads and clears it).
 Tensor status(int64_t device) { return status_word(at::Device(at::kCUDA, (c10::DeviceIndex)device)); }
 
+// ------------------------------------------------ fused elementwise / row ops
+int32_t dtype16(const Tensor &t) {
+  TORCH_CHECK(t.is_cuda(), "the sm_100a fused ops need CUDA tensors (there is no CPU path)");
+  return dtype_code(t);
+}
+cudaStream_t stream_of(const Tensor &t) { return c10::cuda::getCurrentCUDAStream(t.device().index()).stream(); }
+
+Tensor silu_mul(const Tensor &a_, const Tensor &b_) {
+  TORCH_CHECK(a_.sizes() == b_.sizes() && a_.scalar_type() == b_.scalar_type(), "silu_mul: a and b must match");
+  c10::cuda::CUDAGuard guard(a_.device());
+  const Tensor a = a_.contiguous(), b = b_.contiguous();
+  Tensor out = at::empty_like(a);
+  check(st_silu_mul_fwd(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), dtype16(a), stream_of(a)),
+        "st_silu_mul_fwd");
+  return out;
+}
+
+std::tuple<Tensor, Tensor> silu_mul_bwd(const Tensor &a_, const Tensor &b_, const Tensor &g_) {
+  c10::cuda::CUDAGuard guard(a_.device());
+  const Tensor a = a_.contiguous(), b = b_.contiguous(), g = g_.contiguous().to(a.scalar_type());
+  Tensor da = at::empty_like(a), db = at::empty_like(b);
+  check(st_silu_mul_bwd(a.data_ptr(), b.data_ptr(), g.data_ptr(), da.data_ptr(), db.data_ptr(), a.numel(),
+                        dtype16(a), stream_of(a)),
+        "st_silu_mul_bwd");
+  return {da, db};
+}
+
+std::tuple<Tensor, Tensor> rmsnorm_residual(const Tensor &x_, const Tensor &r_, const Tensor &w_, double eps) {
+  TORCH_CHECK(x_.sizes() == r_.sizes(), "rmsnorm_residual: x and residual must match");
+  TORCH_CHECK(w_.dim() == 1 && w_.size(0) == x_.size(-1), "rmsnorm_residual: weight must be [D]");
+  c10::cuda::CUDAGuard guard(x_.device());
+  const Tensor x = x_.contiguous(), r = r_.contiguous().to(x.scalar_type()), w = w_.contiguous().to(x.scalar_type());
+  const int64_t D = x.size(-1), N = D ? x.numel() / D : 0;
+  Tensor out = at::empty_like(x);
+  Tensor rstd = at::empty(x.sizes().slice(0, x.dim() - 1), x.options().dtype(at::kFloat));
+  check(st_rmsnorm_residual_fwd(x.data_ptr(), r.data_ptr(), w.data_ptr(), out.data_ptr(), rstd.data_ptr<float>(), N,
+                                D, (float)eps, dtype16(x), stream_of(x)),
+        "st_rmsnorm_residual_fwd");
+  return {out, rstd};
+}
+
+std::tuple<Tensor, Tensor> rmsnorm_residual_bwd(const Tensor &x_, const Tensor &w_, const Tensor &rstd_,
+                                                const Tensor &dy_) {
+  c10::cuda::CUDAGuard guard(x_.device());
+  const Tensor x = x_.contiguous(), w = w_.contiguous().to(x.scalar_type()), rstd = rstd_.contiguous(),
+               dy = dy_.contiguous().to(x.scalar_type());
+  const int64_t D = x.size(-1), N = D ? x.numel() / D : 0;
+  Tensor dx = at::empty_like(x);
+  Tensor dw = at::empty({D}, x.options().dtype(at::kFloat));
+  Tensor scratch = at::empty({(int64_t)(st_rmsnorm_residual_bwd_scratch(N, D) / sizeof(float)) + 1},
+                             x.options().dtype(at::kFloat));
+  check(st_rmsnorm_residual_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), dx.data_ptr(),
+                                dw.data_ptr<float>(), scratch.data_ptr<float>(), N, D, dtype16(x), stream_of(x)),
+        "st_rmsnorm_residual_bwd");
+  return {dx, dw};
+}
+
+std::tuple<Tensor, Tensor, Tensor> cross_entropy(const Tensor &logits_, const Tensor &labels_, bool want_probs) {
+  TORCH_CHECK(logits_.dim() == 2, "cross_entropy: logits must be [N, V]");
+  TORCH_CHECK(labels_.dim() == 1 && labels_.size(0) == logits_.size(0), "cross_entropy: labels must be [N]");
+  c10::cuda::CUDAGuard guard(logits_.device());
+  const Tensor logits = logits_.contiguous(), labels = labels_.contiguous().to(at::kLong);
+  const int64_t N = logits.size(0), V = logits.size(1);
+  const auto f32 = logits.options().dtype(at::kFloat);
+  Tensor loss = at::empty({N}, f32), lse = at::empty({N}, f32);
+  Tensor probs = want_probs ? at::empty_like(logits) : at::empty({0}, logits.options());
+  check(st_cross_entropy_fwd(logits.data_ptr(), labels.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                             lse.data_ptr<float>(), want_probs ? probs.data_ptr() : nullptr, N, V, dtype16(logits),
+                             stream_of(logits)),
+        "st_cross_entropy_fwd");
+  return {loss, lse, probs};
+}
+
+Tensor cross_entropy_bwd(const Tensor &logits_, const Tensor &labels_, const Tensor &lse_, const Tensor &dloss_) {
+  c10::cuda::CUDAGuard guard(logits_.device());
+  const Tensor logits = logits_.contiguous(), labels = labels_.contiguous().to(at::kLong), lse = lse_.contiguous(),
+               dloss = dloss_.contiguous().to(at::kFloat);
+  const int64_t N = logits.size(0), V = logits.size(1);
+  Tensor dlogits = at::empty_like(logits);
+  check(st_cross_entropy_bwd(logits.data_ptr(), labels.data_ptr<int64_t>(), lse.data_ptr<float>(),
+                             dloss.data_ptr<float>(), dlogits.data_ptr(), N, V, dtype16(logits), stream_of(logits)),
+        "st_cross_entropy_bwd");
+  return dlogits;
+}
+
 }  // namespace
+
+TORCH_LIBRARY(st_b200, m) {
+  m.def("silu_mul(Tensor a, Tensor b) -> Tensor");
+  m.def("silu_mul_bwd(Tensor a, Tensor b, Tensor dout) -> (Tensor, Tensor)");
+  m.def("rmsnorm_residual(Tensor x, Tensor residual, Tensor weight, float eps) -> (Tensor, Tensor)");
+  m.def("rmsnorm_residual_bwd(Tensor x, Tensor weight, Tensor rstd, Tensor dy) -> (Tensor, Tensor)");
+  m.def("cross_entropy(Tensor logits, Tensor labels, bool want_probs) -> (Tensor, Tensor, Tensor)");
+  m.def("cross_entropy_bwd(Tensor logits, Tensor labels, Tensor lse, Tensor dloss) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(st_b200, CUDA, m) {
+  m.impl("silu_mul", &silu_mul);
+  m.impl("silu_mul_bwd", &silu_mul_bwd);
+  m.impl("rmsnorm_residual", &rmsnorm_residual);
+  m.impl("rmsnorm_residual_bwd", &rmsnorm_residual_bwd);
+  m.impl("cross_entropy", &cross_entropy);
+  m.impl("cross_entropy_bwd", &cross_entropy_bwd);
+}
 
 TORCH_LIBRARY(kda_b200, m) {
   m.def(

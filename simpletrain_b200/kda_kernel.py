@@ -104,16 +104,29 @@ def kda_chunked_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def install() -> None:
-    """Route SimpleTrain's ``kernels.kda_kernel`` imports to this module.
+    """Route SimpleTrain's ``kernels.kda_kernel`` imports to this module and
+    ``kernels.fused_ops`` imports to ``simpletrain_b200.fused_ops``.
 
     Call before importing ``models.kimi_k3``; an already imported
-    ``models.kimi_k3`` has its ``kda_chunked_scan`` name rebound too.
+    ``models.kimi_k3`` has its ``kda_chunked_scan`` and fused-op names rebound too.
     """
+    import importlib
+    import types
+
     me = sys.modules[__name__]
+    from . import fused_ops as fo
+    try:
+        pkg = importlib.import_module("kernels")
+    except ModuleNotFoundError:  # SimpleTrain not on sys.path: a bare package to hang the modules on
+        pkg = types.ModuleType("kernels")
+        pkg.__path__ = []
+        sys.modules["kernels"] = pkg
     sys.modules["kernels.kda_kernel"] = me
-    pkg = sys.modules.get("kernels")
-    if pkg is not None:
-        setattr(pkg, "kda_kernel", me)
+    sys.modules["kernels.fused_ops"] = fo
+    setattr(pkg, "kda_kernel", me)
+    setattr(pkg, "fused_ops", fo)
     model = sys.modules.get("models.kimi_k3")
     if model is not None:
         setattr(model, "kda_chunked_scan", kda_chunked_scan)
+        for name in ("fused_silu_mul", "fused_rmsnorm_residual", "fused_cross_entropy"):
+            setattr(model, name, getattr(fo, name))

@@ -13,12 +13,14 @@ from simpletrain_b200 import _ffi
 
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
 HEADER = os.path.join(ROOT, "include", "kda_sm100.h")
+HEADERS = (HEADER, os.path.join(ROOT, "include", "st_fused_ops.h"))
 
 
 def _declared_functions():
-    src = open(HEADER).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    names = re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(kda_[a-z0-9_]+)\s*\(", src, flags=re.M)
+    names = []
+    for h in HEADERS:
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*((?:kda|st)_[a-z0-9_]+)\s*\(", src, flags=re.M)
     return sorted(set(names))
 
 
