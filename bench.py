@@ -428,6 +428,61 @@ def run_reference(args, w, rank, world):
     }
 
 
+def run_fused_ops(args):
+    """One JSON line per fused op (fwd and bwd): HBM GB/s against the measured peak.
+
+    Shapes are the 1b model's: tokens N = 16 x 2048, d_model 2560, FFN hidden
+    6912, vocabulary 32000; bf16.  Algorithmic bytes = every operand read and
+    written once.  Inputs exceed L2.
+    """
+    import simpletrain_b200.fused_ops  # noqa: F401  (loads the ops)
+    peak = load_peaks()["hbm_gbs"]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    N, Dm, Hf, V = 16 * 2048, 2560, 6912, 32000
+    bf = torch.bfloat16
+
+    def mk(*shape):
+        return torch.randn(*shape, generator=g).to(bf).to(dev)
+
+    def timed(fn, n=50):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    ops = torch.ops.st_b200
+    a, bb, dout = mk(N, Hf), mk(N, Hf), mk(N, Hf)
+    x, r, dy, w = mk(N, Dm), mk(N, Dm), mk(N, Dm), mk(Dm)
+    _, rstd = ops.rmsnorm_residual(x, r, w, 1e-6)
+    logits = mk(N // 2, V)
+    labels = torch.randint(0, V, (N // 2,), generator=g).to(dev)
+    _, lse, _ = ops.cross_entropy(logits, labels, False)
+    dl = torch.full((N // 2,), 1.0 / (N // 2), device=dev)
+    e = 2  # bytes per bf16 element
+    cases = [
+        ("silu_mul fwd", lambda: ops.silu_mul(a, bb), 3 * N * Hf * e),
+        ("silu_mul bwd", lambda: ops.silu_mul_bwd(a, bb, dout), 5 * N * Hf * e),
+        ("rmsnorm_residual fwd", lambda: ops.rmsnorm_residual(x, r, w, 1e-6), 3 * N * Dm * e),
+        ("rmsnorm_residual bwd", lambda: ops.rmsnorm_residual_bwd(x, w, rstd, dy), 3 * N * Dm * e),
+        ("cross_entropy fwd (loss only)", lambda: ops.cross_entropy(logits, labels, False), (N // 2) * V * e),
+        ("cross_entropy fwd (+softmax)", lambda: ops.cross_entropy(logits, labels, True), 2 * (N // 2) * V * e),
+        ("cross_entropy bwd", lambda: ops.cross_entropy_bwd(logits, labels, lse, dl), 2 * (N // 2) * V * e),
+    ]
+    for name, fn, nbytes in cases:
+        ms = timed(fn)
+        gbs = nbytes / ms / 1e6
+        print(json.dumps({"op": name, "ms": round(ms, 4), "GB_s": round(gbs, 1), "peak_GB_s": peak,
+                          "frac": round(gbs / peak, 4), "algorithmic_bytes": nbytes,
+                          "shape": {"tokens": N, "d_model": Dm, "ffn_hidden": Hf, "vocab": V}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,8 +497,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--fused-ops", action="store_true",
+                    help="measure the fused silu*mul / RMSNorm / cross-entropy ops instead (one line each)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.fused_ops:
+        run_fused_ops(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

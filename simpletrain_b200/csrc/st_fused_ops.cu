@@ -6,11 +6,12 @@
 // (eight 16-bit values), fp32 arithmetic, and grids sized to the SM count.
 //   silu * mul      elementwise, grid-stride            (kernels/fused_ops.py:62-81)
 //   RMSNorm + res   one warp per row, two sweeps of the row (the second hits
-//                   L2); the weight gradient is reduced per CTA in shared
-//                   memory, then across CTAs          (kernels/fused_ops.py:129-145)
-//   cross-entropy   one CTA per row, online max / sum over the vocabulary,
-//                   optional softmax sweep; the backward recomputes
-//                   softmax from the saved log-sum-exp  (kernels/fused_ops.py:209-263)
+//                   L2); the weight gradient is summed per CTA in registers,
+//                   then across CTAs in a fixed order  (kernels/fused_ops.py:129-145)
+//   cross-entropy   one CTA per row: a max sweep over the vocabulary from HBM,
+//                   a sum-of-exp sweep that hits L2, an optional softmax
+//                   sweep; the backward recomputes softmax from the saved
+//                   log-sum-exp                        (kernels/fused_ops.py:209-263)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -180,13 +181,79 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
-// Persistent CTAs walk rows grid-stride (one warp per row at a time); each CTA
-// sums dy * x * rstd over its rows into shared memory and writes the partial.
-// dx_i = rstd w_i dy_i - rstd^3 / D * x_i * sum_j x_j w_j dy_j.
-template <bool BF>
+// Persistent CTAs walk tiles of 8 rows grid-stride.  Per tile: each warp
+// reduces one row's sum_j x_j w_j dy_j (kept in shared memory), then all 256
+// threads sweep the tile's columns in 16-byte vectors, writing
+//   dx_i = rstd w_i dy_i - rstd^3 / D * x_i * sum_j x_j w_j dy_j
+// and adding dy_i x_i rstd into per-thread weight-gradient registers (thread
+// t owns column vectors t, t + 256, ...).  Each CTA writes its partial at the
+// end.  D % 8 == 0 and 16-byte aligned rows (else the scalar variant).
+template <bool BF, int NV>
 __global__ void __launch_bounds__(kBlock)
     rmsnorm_bwd_kernel(const void *x, const void *w, const float *rstd, const void *dy, void *dx, float *partials,
                        int64_t N, int64_t D) {
+  constexpr int R = kBlock / 32;  // rows per tile
+  __shared__ float sm_c[R], sm_rs[R];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t DV = D / 8;
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x), *g4 = reinterpret_cast<const uint4 *>(dy),
+              *w4 = reinterpret_cast<const uint4 *>(w);
+  uint4 *dx4 = reinterpret_cast<uint4 *>(dx);
+  float acc[NV][8];
+  for (int k = 0; k < NV; ++k)
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+  for (int64_t r0 = (int64_t)blockIdx.x * R; r0 < N; r0 += (int64_t)gridDim.x * R) {
+    const int64_t row = r0 + warp;
+    if (row < N) {
+      float dot = 0.f;
+      for (int64_t v = lane; v < DV; v += 32) {
+        float fx[8], fg[8], fw[8];
+        unpack8<BF>(__ldg(x4 + row * DV + v), fx);
+        unpack8<BF>(__ldg(g4 + row * DV + v), fg);
+        unpack8<BF>(__ldg(w4 + v), fw);
+        for (int j = 0; j < 8; ++j) dot = fmaf(fx[j] * fw[j], fg[j], dot);
+      }
+      dot = warp_sum(dot);
+      if (lane == 0) {
+        const float rs = rstd[row];
+        sm_rs[warp] = rs;
+        sm_c[warp] = rs * rs * rs * dot / (float)D;
+      }
+    }
+    __syncthreads();
+    const int nr = (int)((N - r0) < R ? (N - r0) : R);
+    for (int rr = 0; rr < nr; ++rr) {
+      const int64_t rb = (r0 + rr) * DV;
+      const float rs = sm_rs[rr], c = sm_c[rr];
+      for (int k = 0; k < NV; ++k) {
+        const int64_t v = threadIdx.x + (int64_t)kBlock * k;
+        if (v < DV) {
+          float fx[8], fg[8], fw[8], fo[8];
+          unpack8<BF>(__ldg(x4 + rb + v), fx);  // L1 / L2: read by the dot pass just before
+          unpack8<BF>(__ldg(g4 + rb + v), fg);
+          unpack8<BF>(__ldg(w4 + v), fw);
+          for (int j = 0; j < 8; ++j) {
+            fo[j] = rs * fw[j] * fg[j] - c * fx[j];
+            acc[k][j] = fmaf(fg[j] * fx[j], rs, acc[k][j]);
+          }
+          dx4[rb + v] = pack8<BF>(fo);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int k = 0; k < NV; ++k) {
+    const int64_t v = threadIdx.x + (int64_t)kBlock * k;
+    if (v < DV)
+      for (int j = 0; j < 8; ++j) partials[(int64_t)blockIdx.x * D + 8 * v + j] = acc[k][j];
+  }
+}
+
+// scalar variant (any D): warp per row, shared-memory weight-gradient sums
+template <bool BF>
+__global__ void __launch_bounds__(kBlock)
+    rmsnorm_bwd_scalar_kernel(const void *x, const void *w, const float *rstd, const void *dy, void *dx,
+                              float *partials, int64_t N, int64_t D) {
   extern __shared__ float dw_acc[];  // [D]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t i = threadIdx.x; i < D; i += kBlock) dw_acc[i] = 0.f;
@@ -195,16 +262,14 @@ __global__ void __launch_bounds__(kBlock)
     const int64_t base = row * D;
     const float rs = rstd[row];
     float dot = 0.f;
-    for (int64_t i = lane; i < D; i += 32) {
-      const float xv = load1<BF>(x, base + i), gv = load1<BF>(dy, base + i);
-      dot = fmaf(xv * load1<BF>(w, i), gv, dot);
-      atomicAdd(&dw_acc[i], gv * xv * rs);  // shared-memory atomics: one row per warp at a time
-    }
+    for (int64_t i = lane; i < D; i += 32)
+      dot = fmaf(load1<BF>(x, base + i) * load1<BF>(w, i), load1<BF>(dy, base + i), dot);
     dot = warp_sum(dot);
     const float c = rs * rs * rs * dot / (float)D;
     for (int64_t i = lane; i < D; i += 32) {
       const float xv = load1<BF>(x, base + i), gv = load1<BF>(dy, base + i);
       store1<BF>(dx, base + i, rs * load1<BF>(w, i) * gv - c * xv);
+      atomicAdd(&dw_acc[i], gv * xv * rs);
     }
   }
   __syncthreads();
@@ -226,58 +291,57 @@ int rmsnorm_bwd_grid(int64_t N) {
 }
 
 // ---------------------------------------------------------- cross-entropy
-// (m, s) of a running log-sum-exp: value = m + log(s)
-__device__ __forceinline__ void lse_merge(float &m, float &s, float m2, float s2) {
-  const float mm = fmaxf(m, m2);
-  if (mm == -INFINITY) return;
-  s = s * expf(m - mm) + s2 * expf(m2 - mm);
-  m = mm;
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sm) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sm[0];
+  for (int i = 1; i < kBlock / 32; ++i) r = is_max ? fmaxf(r, sm[i]) : r + sm[i];
+  __syncthreads();  // sm is reused by the next reduction
+  return r;
 }
 
 template <bool BF, bool VEC>
 __global__ void __launch_bounds__(kBlock)
     ce_fwd_kernel(const void *logits, const int64_t *labels, float *loss, float *lse_out, void *probs, int64_t V) {
-  __shared__ float sm_m[kBlock / 32], sm_s[kBlock / 32];
-  __shared__ float sh_lse;
+  __shared__ float sm[kBlock / 32];
   const int64_t row = blockIdx.x, base = row * V;
-  float m = -INFINITY, s = 0.f;
+  const uint4 *l4 = reinterpret_cast<const uint4 *>(logits) + base / 8;
+  // sweep 1 (HBM): the row maximum
+  float m = -INFINITY;
   if (VEC) {
-    const uint4 *l4 = reinterpret_cast<const uint4 *>(logits) + base / 8;
     for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
       float f[8];
       unpack8<BF>(__ldg(l4 + i), f);
-      float bm = f[0];
-      for (int k = 1; k < 8; ++k) bm = fmaxf(bm, f[k]);
-      float bs = 0.f;
-      for (int k = 0; k < 8; ++k) bs += expf(f[k] - bm);
-      lse_merge(m, s, bm, bs);
+      for (int k = 0; k < 8; ++k) m = fmaxf(m, f[k]);
     }
   } else {
-    for (int64_t i = threadIdx.x; i < V; i += kBlock) lse_merge(m, s, load1<BF>(logits, base + i), 1.f);
+    for (int64_t i = threadIdx.x; i < V; i += kBlock) m = fmaxf(m, load1<BF>(logits, base + i));
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    lse_merge(m, s, m2, s2);
+  m = block_reduce(m, true, sm);
+  // sweep 2 (L2): sum of exp(x - max)
+  float s = 0.f;
+  if (VEC) {
+    for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
+      float f[8];
+      unpack8<BF>(__ldg(l4 + i), f);
+      for (int k = 0; k < 8; ++k) s += expf(f[k] - m);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += kBlock) s += expf(load1<BF>(logits, base + i) - m);
   }
-  if ((threadIdx.x & 31) == 0) {
-    sm_m[threadIdx.x >> 5] = m;
-    sm_s[threadIdx.x >> 5] = s;
-  }
-  __syncthreads();
+  s = block_reduce(s, false, sm);
+  const float l = m + logf(s);
   if (threadIdx.x == 0) {
-    float mm = sm_m[0], ss = sm_s[0];
-    for (int i = 1; i < kBlock / 32; ++i) lse_merge(mm, ss, sm_m[i], sm_s[i]);
-    const float l = mm + logf(ss);
-    sh_lse = l;
     lse_out[row] = l;
     const int64_t lab = labels[row];
     loss[row] = (lab >= 0 && lab < V) ? l - load1<BF>(logits, base + lab) : NAN;  // out-of-range label: NaN
   }
   if (probs == nullptr) return;
-  __syncthreads();
-  const float l = sh_lse;
   if (VEC) {
-    const uint4 *l4 = reinterpret_cast<const uint4 *>(logits) + base / 8;
     uint4 *p4 = reinterpret_cast<uint4 *>(probs) + base / 8;
     for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
       float f[8];
@@ -391,22 +455,37 @@ int st_rmsnorm_residual_bwd(const void *x, const void *weight, const float *rstd
                             kda_stream_t stream) {
   if (N < 0 || D <= 0) return KDA_ERR_BAD_SHAPE;
   if (!dtype_ok(dtype)) return KDA_ERR_UNSUPPORTED;
-  if ((size_t)D * sizeof(float) > 200 * 1024) return KDA_ERR_UNSUPPORTED;  // the weight gradient lives in smem
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (N == 0) return status_of(cudaMemsetAsync(dweight, 0, (size_t)D * sizeof(float), st));
   if (!x || !weight || !rstd || !dy || !dx || !dweight || !partials) return KDA_ERR_NULL_ARGUMENT;
   const int grid = rmsnorm_bwd_grid(N);
-  const size_t smem = (size_t)D * sizeof(float);
-  cudaError_t e = cudaSuccess;
-  if (dtype == KDA_DTYPE_BF16) {
-    e = cudaFuncSetAttribute(rmsnorm_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      rmsnorm_bwd_kernel<true><<<grid, kBlock, smem, st>>>(x, weight, rstd, dy, dx, partials, N, D);
+  const bool bf = dtype == KDA_DTYPE_BF16;
+  const bool vec = D % 8 == 0 && aligned16(x) && aligned16(weight) && aligned16(dy) && aligned16(dx);
+  const int nvec = (int)((D / 8 + kBlock - 1) / kBlock);
+  if (vec && nvec <= 8) {
+#define ST_RMS_BWD(NC)                                                                                        \
+  if (nvec <= NC) {                                                                                         \
+    if (bf) rmsnorm_bwd_kernel<true, NC><<<grid, kBlock, 0, st>>>(x, weight, rstd, dy, dx, partials, N, D); \
+    else rmsnorm_bwd_kernel<false, NC><<<grid, kBlock, 0, st>>>(x, weight, rstd, dy, dx, partials, N, D);   \
+  } else
+    ST_RMS_BWD(1) ST_RMS_BWD(2) ST_RMS_BWD(4) ST_RMS_BWD(8) {}
+#undef ST_RMS_BWD
   } else {
-    e = cudaFuncSetAttribute(rmsnorm_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      rmsnorm_bwd_kernel<false><<<grid, kBlock, smem, st>>>(x, weight, rstd, dy, dx, partials, N, D);
+    const size_t smem = (size_t)D * sizeof(float);
+    if (smem > 200 * 1024) return KDA_ERR_UNSUPPORTED;
+    cudaError_t e0;
+    if (bf) {
+      e0 = cudaFuncSetAttribute(rmsnorm_bwd_scalar_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e0 == cudaSuccess)
+        rmsnorm_bwd_scalar_kernel<true><<<grid, kBlock, smem, st>>>(x, weight, rstd, dy, dx, partials, N, D);
+    } else {
+      e0 = cudaFuncSetAttribute(rmsnorm_bwd_scalar_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e0 == cudaSuccess)
+        rmsnorm_bwd_scalar_kernel<false><<<grid, kBlock, smem, st>>>(x, weight, rstd, dy, dx, partials, N, D);
+    }
+    if (e0 != cudaSuccess) return status_of(e0);
   }
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return status_of(e);
   const int g2 = (int)((D + kBlock - 1) / kBlock);
   sum_rows_kernel<<<g2 < 1024 ? g2 : 1024, kBlock, 0, st>>>(partials, dweight, grid, D);
