@@ -309,3 +309,22 @@ def test_long_context_split_consistency():
     y2, S2 = kda_chunk(q[:, :, h:], k[:, :, h:], v[:, :, h:], g[:, :, h:], decay, S1)
     assert max_rel(torch.cat([y1, y2], 2).float(), y.float()) <= TOL_LOWP
     assert max_rel(S2, S) <= TOL_STATE
+
+
+def test_layer_glue_after_the_scan_copies_nothing():
+    """The KDA layer (models/kimi_k3.py:99-124) views [B, T, H*Dh] projections
+    as [B, H, T, Dh], scales the scan output per head and returns
+    ``o.transpose(1, 2).contiguous()``.  The scan writes y in its inputs' memory
+    order ([B, T, H, Dh]), so the head scale keeps that order and the final
+    ``contiguous()`` is a no-op instead of a full copy of y."""
+    B, T, H, Dh = 2, 256, 4, 64
+    g = torch.Generator().manual_seed(7)
+    proj = [torch.randn(B, T, H * Dh, generator=g).to(torch.bfloat16).to(DEV) for _ in range(4)]
+    q, k, v, gate = (p.view(B, T, H, Dh).transpose(1, 2) for p in proj)
+    o = kda_chunked_scan(q, k, v, gate=gate, decay=0.97, chunk_size=64)
+    assert o.stride() == q.stride()
+    head_scale = torch.rand(H, device=DEV)
+    o = o * head_scale.view(1, H, 1, 1).to(o.dtype)
+    t = o.transpose(1, 2)
+    assert t.is_contiguous()
+    assert t.contiguous().data_ptr() == o.data_ptr()
