@@ -150,14 +150,20 @@ def run_ours(args, w, rank, world, local_rank):
     inp = make_inputs(w, seed=rank, device=dev)
     q, k, v, g, dy, decay, s0 = (inp[n] for n in ("q", "k", "v", "g", "dy", "decay", "s0"))
     B, H, T, D = w.B, w.H, w.T, w.D
-    dec = decay.expand(B, H, D)
+    if args.per_step:
+        # per-token decay, one value per head (the first channel's)
+        mode, need_dd = 2, False
+        dec = decay[:, :1].expand(B, H, D)
+    else:
+        mode, need_dd = 0, True
+        dec = decay.expand(B, H, D)
     fwd = torch.ops.kda_b200.chunk_fwd
     bwd = torch.ops.kda_b200.chunk_bwd
 
     def step():
-        y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, False, True)
+        y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, mode, True)
         if w.backward:
-            return bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, False, True, s0 is not None)
+            return bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, mode, need_dd, s0 is not None)
         return y
 
     def barrier():
@@ -192,10 +198,10 @@ def run_ours(args, w, rank, world, local_rank):
         for i in range(steps):
             e0, e1, e2 = ev[i]
             e0.record(stream)
-            y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, False, True)
+            y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, mode, True)
             e1.record(stream)
             if w.backward:
-                bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, False, True, s0 is not None)
+                bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, mode, need_dd, s0 is not None)
             e2.record(stream)
         end.record(stream)
         torch.cuda.synchronize()
@@ -242,7 +248,10 @@ def run_ours(args, w, rank, world, local_rank):
 
     # ---- CPU baseline (rank 0, N = 1) ----------------------------------------------
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if args.per_step:
+        cpu = {"unavailable": "the reference has no CPU implementation of per-step decay "
+                              "(only its never-launched Triton kernel describes it)"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, budget_s=args.cpu_seconds)
 
     return {
@@ -252,6 +261,7 @@ def run_ours(args, w, rank, world, local_rank):
         "data": "synthetic (seeded; q,k L2-normalised N(0,1), v N(0,1), g sigmoid(N(0,1)), "
                 "per-channel decay sigmoid(N(3,1)))",
         "config": dict(w.describe(), global_batch=w.B * world, seq_len=w.T,
+                       semantics="per-step decay (one per head)" if args.per_step else "chunk-constant decay",
                        parallelism=f"(batch,head) shards, {world} rank(s), no data-path collective",
                        l2="inputs larger than L2 (no flush needed)"),
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
@@ -285,8 +295,13 @@ def run_e2e(args, w, rank, world, dev, inp):
         nonlocal outs, d2h
         for n in names + ["decay"]:
             dev_in[n].copy_(host[n], non_blocking=True)
-        leaves = [dev_in[n].requires_grad_(True) for n in ("q", "k", "v", "g", "decay")]
-        y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], inp["s0"])
+        if args.per_step:  # one decay per head, not differentiated
+            leaves = [dev_in[n].requires_grad_(True) for n in ("q", "k", "v", "g")]
+            y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], dev_in["decay"][:, 0], inp["s0"],
+                             per_step=True)
+        else:
+            leaves = [dev_in[n].requires_grad_(True) for n in ("q", "k", "v", "g", "decay")]
+            y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], inp["s0"])
         grads = torch.autograd.grad([y], leaves, [dev_in["dy"]])
         res = [y] + list(grads)
         if outs is None:
@@ -493,6 +508,8 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="B,H,T,D: run a custom shape (profiling / sweeps) instead of --workload")
     ap.add_argument("--fwd-only", action="store_true", help="with --shape: forward pass only")
+    ap.add_argument("--per-step", action="store_true",
+                    help="per-token decay semantics (one decay per head) instead of chunk-constant decay")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 1
+#define KDA_ABI_VERSION 2
 
 typedef struct CUstream_st *kda_stream_t; /* identical to cudaStream_t */
 
@@ -58,13 +58,22 @@ enum kda_flags {
   /* Reference-exact state update U_c = K_c V_c^T (kernels/kda_kernel.py:294).
      Needs D == chunk; a ragged last chunk may not ask for the final state. */
   KDA_FLAG_LITERAL = 1u << 0,
+  /* Per-token decay instead of the chunk-constant one (ABI version 2): the
+     recurrence of the reference's docstring and Triton kernel
+     (kernels/kda_kernel.py:8-11, :134-180)
+         s_t = a s_{t-1} + k_t^T v_t,   o_t = q_t s_t,   y_t = g_t * o_t
+     with one decay a per (batch, head): decay == NULL (decay_scalar) or
+     decay_stride_d == 0, and 0.125 <= a <= 1 (checked for decay_scalar; the
+     kernels scale q and k rows by powers of a up to a^-32).  state_out is
+     s_T.  Not with KDA_FLAG_LITERAL; kda_bwd_sm100 takes ddecay == NULL. */
+  KDA_FLAG_PER_STEP = 1u << 1,
 };
 
 enum kda_status {
   KDA_OK = 0,
   KDA_ERR_NULL_ARGUMENT = 1,   /* a required pointer is NULL */
   KDA_ERR_BAD_SHAPE = 2,       /* negative size, or literal mode with D != chunk */
-  KDA_ERR_UNSUPPORTED = 3,     /* head dim / chunk / dtype this build has no kernel for */
+  KDA_ERR_UNSUPPORTED = 3,     /* head dim / chunk / dtype / flag combination without a kernel */
   KDA_ERR_BAD_LAYOUT = 4,      /* stride or alignment rule violated */
   KDA_ERR_WORKSPACE = 5,       /* workspace missing or too small */
   KDA_ERR_CUDA = 6,            /* a CUDA runtime call or launch failed */

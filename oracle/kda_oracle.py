@@ -243,3 +243,154 @@ def manual_backward(q, k, v, gate, decay_bhd: torch.Tensor, chunk_size: int,
 
     d_decay = torch.where(a != 0, dlog / torch.where(a != 0, a, torch.ones_like(a)), torch.zeros_like(a))
     return dq, dk, dv, dg, d_decay, dS0
+
+
+# --------------------------------------------------------------------------- #
+# per-step (docstring) semantics
+# --------------------------------------------------------------------------- #
+# The reference's module docstring (kernels/kda_kernel.py:8-11), its README
+# (README.md:83-87) and its never-launched Triton kernel (:134-180) describe a
+# per-token recurrence instead of the chunk-constant torch loop:
+#
+#     s_t = a * s_{t-1} + k_t^T v_t,   o_t = q_t s_t,   y_t = g_t * o_t
+#
+# with one scalar decay a.  (The Triton kernel also multiplies the state by a
+# once more after the last token before storing it, :172-189; the final state
+# here is s_T, the value the recurrence defines and the one a continuation
+# starts from.)
+REF_ROW = 32  # reference row of the scaled operands (see per_step_chunk_scan)
+
+
+def _decay_bh(decay, B: int, H: int) -> torch.Tensor:
+    """Per-step decay as a float64 [B, H] tensor (float, (), (H,), or broadcastable to (B, H))."""
+    if not torch.is_tensor(decay):
+        return torch.full((B, H), float(decay), dtype=torch.float64)
+    d = decay.double()
+    if d.dim() == 1 and d.shape[0] == H:
+        d = d.view(1, H)
+    return torch.broadcast_to(d, (B, H)).clone()
+
+
+def per_step_recurrence(q, k, v, gate, decay, initial_state: Optional[torch.Tensor] = None):
+    """The per-token recurrence itself, in float64 (small cases): (y, s_T).
+
+    Differentiable by autograd; the known answer for the per-step kernels.
+    """
+    B, H, T, D = q.shape
+    qd, kd, vd = q.double(), k.double(), v.double()
+    gd = gate.double() if gate is not None else None
+    a = _decay_bh(decay, B, H)[:, :, None, None]
+    S = torch.zeros(B, H, D, D, dtype=torch.float64) if initial_state is None else initial_state.double()
+    ys = []
+    for t in range(T):
+        S = a * S + kd[:, :, t, :, None] * vd[:, :, t, None, :]
+        o = torch.einsum("bhd,bhde->bhe", qd[:, :, t], S)
+        ys.append(o * gd[:, :, t] if gd is not None else o)
+    y = torch.stack(ys, dim=2) if ys else torch.zeros(B, H, 0, D, dtype=torch.float64)
+    return y, S
+
+
+def _row_factors(a: torch.Tensor, n: int, chunk_size: int):
+    """fq[b,h,i] = a^(i+1-REF_ROW), fk[b,h,j] = a^(REF_ROW-1-j) for rows 0..n-1."""
+    i = torch.arange(n, dtype=torch.float64)
+    fq = a[:, :, None] ** (i + 1 - REF_ROW)
+    fk = a[:, :, None] ** (REF_ROW - 1 - i)
+    return fq, fk
+
+
+def per_step_chunk_scan(q, k, v, gate, decay, chunk_size: int = 64,
+                        initial_state: Optional[torch.Tensor] = None):
+    """Chunked form of the per-step recurrence that the sm_100a kernels run (float64).
+
+    Inside a chunk (local rows i, j < L), with m = REF_ROW,
+
+        Q^ = diag(a^(i+1-m)) Q,   K~ = diag(a^(m-1-j)) K   (so q^_i . k~_j = a^(i-j) q_i . k_j)
+        O  = tril(Q^ K~^T) V + Q^ (a^m S)
+        S' = a^L S + a^(L-m) K~^T V
+
+    i.e. the chunk-constant kernels' products on row-scaled q and k tiles,
+    with scalar factors on the carried state.  Every factor lies in
+    [a^(m), a^(-m)], which is why the kernels take 0.125 <= a <= 1.
+    """
+    B, H, T, D = q.shape
+    C, m = chunk_size, REF_ROW
+    f = torch.float64
+    Q, K, V = q.to(f), k.to(f), v.to(f)
+    G = gate.to(f) if gate is not None else None
+    a = _decay_bh(decay, B, H)
+    a4 = a[:, :, None, None]
+    S = torch.zeros(B, H, D, D, dtype=f) if initial_state is None else initial_state.to(f).clone()
+    fq, fk = _row_factors(a, C, C)
+    causal = torch.ones(C, C, dtype=f).tril()
+    y = torch.zeros(B, H, T, D, dtype=f)
+    for t0 in range(0, T, C):
+        t1 = min(T, t0 + C)
+        L = t1 - t0
+        Qh = Q[:, :, t0:t1] * fq[:, :, :L, None]
+        Kt = K[:, :, t0:t1] * fk[:, :, :L, None]
+        Vc = V[:, :, t0:t1]
+        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        O = P @ Vc + Qh @ (a4 ** m * S)
+        y[:, :, t0:t1] = O * G[:, :, t0:t1] if G is not None else O
+        S = a4 ** L * S + a4 ** (L - m) * (Kt.transpose(-1, -2) @ Vc)
+    return y, S
+
+
+def per_step_manual_backward(q, k, v, gate, decay, chunk_size: int,
+                             initial_state: Optional[torch.Tensor], dy: torch.Tensor,
+                             dstate_T: Optional[torch.Tensor] = None):
+    """Explicit backward of ``per_step_chunk_scan`` -- the algorithm of the kernels (float64).
+
+    Gradients of  L = <dy, y> + <dstate_T, s_T>.  With dO = g * dy, the row
+    factors fq, fk and m = REF_ROW:
+
+      forward direction:  dg = dy * O
+                          dq = diag(fq) [tril(dO V^T) K~ + dO (a^m S_{c-1})^T]
+      reverse direction:  dk = diag(fk) [tril(dO V^T)^T Q^ + V (a^(L-m) dS_c)^T]
+                          dv = tril(Q^ K~^T)^T dO + K~ (a^(L-m) dS_c)
+                          dS_{c-1} = a^L dS_c + a^m Q^^T dO
+
+    Returns (dq, dk, dv, dg, d_initial_state); the decay is not differentiated.
+    """
+    B, H, T, D = q.shape
+    C, m = chunk_size, REF_ROW
+    f = torch.float64
+    Q, K, V = q.to(f), k.to(f), v.to(f)
+    G = gate.to(f) if gate is not None else None
+    DY = dy.to(f)
+    a = _decay_bh(decay, B, H)
+    a4 = a[:, :, None, None]
+    S = torch.zeros(B, H, D, D, dtype=f) if initial_state is None else initial_state.to(f).clone()
+    fq, fk = _row_factors(a, C, C)
+    causal = torch.ones(C, C, dtype=f).tril()
+    chunks = [(t0, min(T, t0 + C)) for t0 in range(0, T, C)]
+    dq = torch.zeros_like(Q); dk = torch.zeros_like(K); dv = torch.zeros_like(V)
+    dg = torch.zeros_like(Q) if G is not None else None
+
+    def tiles(t0, t1):
+        L = t1 - t0
+        Qh = Q[:, :, t0:t1] * fq[:, :, :L, None]
+        Kt = K[:, :, t0:t1] * fk[:, :, :L, None]
+        dO = DY[:, :, t0:t1] * G[:, :, t0:t1] if G is not None else DY[:, :, t0:t1]
+        return L, Qh, Kt, V[:, :, t0:t1], dO
+
+    for (t0, t1) in chunks:
+        L, Qh, Kt, Vc, dO = tiles(t0, t1)
+        Sh = a4 ** m * S
+        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        if G is not None:
+            dg[:, :, t0:t1] = DY[:, :, t0:t1] * (P @ Vc + Qh @ Sh)
+        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        dq[:, :, t0:t1] = fq[:, :, :L, None] * (dP @ Kt + dO @ Sh.transpose(-1, -2))
+        S = a4 ** L * S + a4 ** (L - m) * (Kt.transpose(-1, -2) @ Vc)
+
+    dS = dstate_T.to(f).clone() if dstate_T is not None else torch.zeros(B, H, D, D, dtype=f)
+    for (t0, t1) in reversed(chunks):
+        L, Qh, Kt, Vc, dO = tiles(t0, t1)
+        dSh = a4 ** (L - m) * dS
+        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        dk[:, :, t0:t1] = fk[:, :, :L, None] * (dP.transpose(-1, -2) @ Qh + Vc @ dSh.transpose(-1, -2))
+        dv[:, :, t0:t1] = P.transpose(-1, -2) @ dO + Kt @ dSh
+        dS = a4 ** L * dS + a4 ** m * (Qh.transpose(-1, -2) @ dO)
+    return dq, dk, dv, dg, dS

@@ -10,7 +10,7 @@ import ctypes
 import os
 from ctypes import POINTER, c_char_p, c_double, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 # KDA_B200_LIB_DIR selects another build of both libraries (default: in-tree _lib/)
 LIB_DIR = os.environ.get("KDA_B200_LIB_DIR") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libkda_sm100.so")
@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(LIB_DIR, "libkda_sm100.so")
 KDA_DTYPE_BF16 = 0
 KDA_DTYPE_F16 = 1
 KDA_FLAG_LITERAL = 1 << 0
+KDA_FLAG_PER_STEP = 1 << 1
 
 KDA_OK = 0
 KDA_ERR_NULL_ARGUMENT = 1

@@ -41,9 +41,17 @@ int check_common(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, int3
   if (dtype != KDA_DTYPE_BF16 && dtype != KDA_DTYPE_F16) return KDA_ERR_UNSUPPORTED;
   if (chunk != 64) return KDA_ERR_UNSUPPORTED;
   if (D != 64 && D != 128) return KDA_ERR_UNSUPPORTED;
-  if (flags & ~uint32_t(KDA_FLAG_LITERAL)) return KDA_ERR_UNSUPPORTED;
+  if (flags & ~uint32_t(KDA_FLAG_LITERAL | KDA_FLAG_PER_STEP)) return KDA_ERR_UNSUPPORTED;
+  if ((flags & KDA_FLAG_LITERAL) && (flags & KDA_FLAG_PER_STEP)) return KDA_ERR_UNSUPPORTED;
   if ((flags & KDA_FLAG_LITERAL) && D != chunk) return KDA_ERR_BAD_SHAPE;
   return KDA_OK;
+}
+
+// Per-step mode: one decay per (batch, head) within the range the row scaling allows.
+int check_per_step(uint32_t flags, const float *decay, int64_t stride_d, double scalar) {
+  if (!(flags & KDA_FLAG_PER_STEP)) return KDA_OK;
+  if (decay != nullptr) return stride_d == 0 ? KDA_OK : KDA_ERR_UNSUPPORTED;
+  return (scalar >= 0.125 && scalar <= 1.0) ? KDA_OK : KDA_ERR_UNSUPPORTED;
 }
 
 kda::DecaySrc make_decay(const float *ptr, int64_t sb, int64_t sh, int64_t sd, double scalar, int T,
@@ -92,13 +100,14 @@ int n_ranges(int nstreams, int nchunks, int slots) {
 
 // CTA slots of each kernel on the current device (the launch and the workspace
 // query agree because both ask the same device).
-int fwd_slots(int D, bool literal) {
-  static std::atomic<int> cache[4];  // CTAs per SM by (D == 128, literal); 0 = not asked yet
-  std::atomic<int> &c = cache[(D == 128 ? 2 : 0) + (literal ? 1 : 0)];
+int fwd_slots(int D, uint32_t flags) {
+  const bool literal = (flags & KDA_FLAG_LITERAL) != 0, per_step = (flags & KDA_FLAG_PER_STEP) != 0;
+  static std::atomic<int> cache[8];  // CTAs per SM by (D == 128, literal, per-step); 0 = not asked yet
+  std::atomic<int> &c = cache[(D == 128 ? 4 : 0) + (literal ? 1 : 0) + (per_step ? 2 : 0)];
   int occ = c.load(std::memory_order_relaxed);
   if (occ == 0) {
-    const int a = kda::fwd_tc_occupancy(D, KDA_DTYPE_BF16, literal);
-    const int b = kda::fwd_tc_occupancy(D, KDA_DTYPE_F16, literal);
+    const int a = kda::fwd_tc_occupancy(D, KDA_DTYPE_BF16, literal, per_step);
+    const int b = kda::fwd_tc_occupancy(D, KDA_DTYPE_F16, literal, per_step);
     occ = a > b ? a : b;
     c.store(occ, std::memory_order_relaxed);
   }
@@ -166,7 +175,9 @@ const char *kda_status_string(int32_t s) {
     case KDA_OK: return "ok";
     case KDA_ERR_NULL_ARGUMENT: return "a required pointer argument is NULL";
     case KDA_ERR_BAD_SHAPE: return "invalid shape (negative size, or literal mode with D != chunk)";
-    case KDA_ERR_UNSUPPORTED: return "unsupported configuration (head dim must be 64 or 128, chunk 64, dtype bf16/f16)";
+    case KDA_ERR_UNSUPPORTED:
+      return "unsupported configuration (head dim 64 or 128, chunk 64, dtype bf16/f16; per-step mode: not literal, "
+             "one decay per (batch, head) in [0.125, 1], no decay gradient)";
     case KDA_ERR_BAD_LAYOUT: return "bad layout (innermost stride must be 1, other strides multiples of 8 elements, base 16-byte aligned)";
     case KDA_ERR_WORKSPACE: return "workspace missing or too small";
     case KDA_ERR_CUDA: return "CUDA launch or runtime error";
@@ -177,7 +188,7 @@ const char *kda_status_string(int32_t s) {
 
 size_t kda_fwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, uint32_t flags) {
   if (B <= 0 || H <= 0 || (D != 64 && D != 128)) return 0;
-  const int nc = n_chunks(T, chunk), nr = n_ranges(B * H, nc, fwd_slots(D, (flags & KDA_FLAG_LITERAL) != 0));
+  const int nc = n_chunks(T, chunk), nr = n_ranges(B * H, nc, fwd_slots(D, flags));
   return queue_bytes(nr, carry_f4(D)) + agg_bytes(B * H, nc, nr, carry_f4(D));
 }
 
@@ -197,6 +208,7 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   if (rc) return rc;
   const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   if (literal && p->state_out && (p->T % p->chunk) != 0) return KDA_ERR_BAD_SHAPE;
+  if ((rc = check_per_step(p->flags, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
   if ((p->state_in && !aligned16(p->state_in)) || (p->state_out && !aligned16(p->state_out)))
     return KDA_ERR_BAD_LAYOUT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -219,6 +231,7 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   kda::FwdArgs a{};
   a.B = p->B; a.H = p->H; a.T = p->T; a.D = p->D; a.C = p->chunk;
   a.literal = literal ? 1 : 0;
+  a.per_step = (p->flags & KDA_FLAG_PER_STEP) ? 1 : 0;
   a.q = to_view(p->q); a.k = to_view(p->k); a.v = to_view(p->v); a.g = to_view(p->g); a.y = to_view(p->y);
   a.decay = make_decay(p->decay, p->decay_stride_b, p->decay_stride_h, p->decay_stride_d, p->decay_scalar,
                        p->T, p->chunk);
@@ -226,12 +239,12 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   a.s_out = p->state_out;
   a.status = p->status;
   const int ns = p->B * p->H, nchunks = n_chunks(p->T, p->chunk);
-  const int nr = n_ranges(ns, nchunks, fwd_slots(p->D, literal));
+  const int nr = n_ranges(ns, nchunks, fwd_slots(p->D, p->flags));
   kda::tc::Queue q{};
   void *agg = reinterpret_cast<char *>(p->workspace) + queue_bytes(nr, carry_f4(p->D));
   cudaError_t e = make_queue(q, p->workspace, ns, nchunks, carry_f4(p->D), nr, agg, carry_f4(p->D), st);
   if (e != cudaSuccess) return cuda_status(e);
-  const int slots = fwd_slots(p->D, literal);
+  const int slots = fwd_slots(p->D, p->flags);
   return cuda_status(kda::launch_fwd_tc(a, q, nr < slots ? nr : slots, p->dtype, st));
 }
 
@@ -241,6 +254,8 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   if (rc) return rc;
   const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   if (literal && (p->T % p->chunk) != 0 && p->dstate_out) return KDA_ERR_BAD_SHAPE;
+  if ((rc = check_per_step(p->flags, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
+  if ((p->flags & KDA_FLAG_PER_STEP) && p->ddecay) return KDA_ERR_UNSUPPORTED;
   const bool gate = p->g.data != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->H == 0) return KDA_OK;
@@ -263,6 +278,7 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   kda::BwdArgs a{};
   a.B = p->B; a.H = p->H; a.T = p->T; a.D = p->D; a.C = p->chunk;
   a.literal = literal ? 1 : 0;
+  a.per_step = (p->flags & KDA_FLAG_PER_STEP) ? 1 : 0;
   a.q = to_view(p->q); a.k = to_view(p->k); a.v = to_view(p->v); a.g = to_view(p->g); a.dy = to_view(p->dy);
   a.dq = to_view(p->dq); a.dk = to_view(p->dk); a.dv = to_view(p->dv); a.dg = to_view(p->dg);
   a.decay = make_decay(p->decay, p->decay_stride_b, p->decay_stride_h, p->decay_stride_d, p->decay_scalar,

@@ -21,7 +21,11 @@
 //
 // Warp 0 loads the two tiles of each chunk into a ring, warp 1 issues one
 // UMMA per chunk (K^T V, literal K V^T, or Q^T dO) into one of two TMEM
-// accumulators, warps 2-9 fold it into the fp32 carry in registers.
+// accumulators, warps 2-9 fold it into the fp32 carry in registers.  In
+// per-step mode (PS) warp 10 first scales the rows of the chunk's K (mode 0)
+// or Q (mode 2) tile like the main kernels (kda_tc_epi.cuh, kRef), and the
+// fold applies the scalar factor: S <- a^64 S + a^(64-kRef) K~^T V, or
+// dS <- a^64 dS + a^kRef Q^^T dO.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -42,15 +46,15 @@ struct AggLayout {
   static constexpr int BOX = KB * kTile;
   static constexpr int ST_A = 0, ST_B = BOX, STAGE = 2 * BOX;
   static constexpr int BAR = NS * STAGE;
-  static constexpr int NBAR = 2 * NS + 8;
+  static constexpr int NBAR = 3 * NS + 8;
   static constexpr int TMEM_SLOT = BAR + NBAR * 8;
   static constexpr int ABORT = TMEM_SLOT + 8;
   static constexpr int SMEM = ABORT + 8 + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * D <= 128 ? 128 : 256;  // two accumulators of D columns
 };
 
-template <typename T, int D, bool LIT, int MODE, int NS>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int D, bool LIT, bool PS, int MODE, int NS>
+__global__ void __launch_bounds__(kThreads + (PS ? 32 : 0), 1)
     agg_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const AggArgs a,
                   const Queue qu) {
   using L = AggLayout<D, NS>;
@@ -66,7 +70,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
-  enum { ACC_FULL = 2 * NS, ACC_FREE = ACC_FULL + 2, FIN = ACC_FREE + 2 };
+  enum { ACC_FULL = 2 * NS, ACC_FREE = ACC_FULL + 2, FIN = ACC_FREE + 2, SCALED = FIN + 1 };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,6 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(ACC_FREE + 0), kEpi);
     mbar_init(bar(ACC_FREE + 1), kEpi);
     mbar_init(bar(FIN), 1);
+    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -118,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < n; ++k) {
         const int s = k % NS, use = k / NS, buf = k & 1;
         const uint32_t st = sb + s * L::STAGE;
-        if (!(mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+        if (!(mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
               mbar_wait(bar(ACC_FREE + buf), ((k >> 1) & 1) ^ 1, a.status, abort_flag)))
           break;
         tc_fence_after();
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kThreads / 32) {
     const Epi e;
     Carry<D> S, Tn;
     S.init_rows(e);
@@ -146,6 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     Tn.zero();
     float al[Carry<D>::NR];
     for (int r = 0; r < Carry<D>::NR; ++r) al[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
+    float aw = 1.f;  // per-step factor of each chunk's product
+    if constexpr (PS) aw = pow_log2(log2f(decay_value(a.decay, b, h, 0)), (float)(REV ? kRef : 64 - kRef));
     bool ok = true;
     for (int k = 0; k < n && ok; ++k) {
       const int buf = k & 1;
@@ -158,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) {
             float &sv = S.x[0][16 * sl + i];
             if (MODE == 1) Tn.x[0][16 * sl + i] = al[0] * fmaf(64.f, sv, Tn.x[0][16 * sl + i]);  // T <- a (T + L S)
-            sv = fmaf(al[0], sv, __uint_as_float(u[i]));
+            sv = fmaf(al[0], sv, aw * __uint_as_float(u[i]));
           }
         }
         tc_fence_before();
@@ -173,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = 0; r < Carry<D>::NR; ++r)
           for (int i = 0; i < Carry<D>::NV; ++i) {
             if (MODE == 1) Tn.x[r][i] = al[r] * fmaf(64.f, S.x[r][i], Tn.x[r][i]);  // T <- a (T + L S_prev)
-            S.x[r][i] = fmaf(al[r], S.x[r][i], U.x[r][i]);
+            S.x[r][i] = fmaf(al[r], S.x[r][i], aw * U.x[r][i]);
           }
       }
     }
@@ -181,6 +188,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       float4 *dst = a.agg + (size_t)sp.r * a.agg_f4 * kEpi;
       S.store_slot(e, dst);
       if (MODE == 1) Tn.store_slot(e, dst + (Carry<D>::FLOATS / 4) * kEpi);
+    }
+  } else if constexpr (PS) {
+    // row scaler: K~ rows a^(kRef-1-j) (mode 0) or Q^ rows a^(i+1-kRef) (mode 2) of tile A
+    const float l2a = log2f(decay_value(a.decay, b, h, 0));
+    const float e0 = REV ? (float)(lane + 1 - kRef) : (float)(kRef - 1 - lane);
+    const float f0 = pow_log2(l2a, e0), f1 = pow_log2(l2a, REV ? e0 + 32.f : e0 - 32.f);
+    for (int k = 0; k < n; ++k) {
+      const int s = k % NS, use = k / NS;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
+      scale_tile_rows<L::KB, BF>(sb + s * L::STAGE + L::ST_A, lane, f0, f1);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(SCALED + s));
     }
   }
   __syncthreads();
@@ -190,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int D, bool LIT, int MODE>
+template <typename T, int D, bool LIT, bool PS, int MODE>
 cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Queue &q, cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NS = 4;
@@ -198,10 +218,10 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
   if (!make_tmap_bhtd(&ma, va, a.B, a.H, a.T, D, BF) || !make_tmap_bhtd(&mb, vb, a.B, a.H, a.T, D, BF))
     return cudaErrorInvalidValue;
   using L = AggLayout<D, NS>;
-  auto kern = agg_tc_kernel<T, D, LIT, MODE, NS>;
+  auto kern = agg_tc_kernel<T, D, LIT, PS, MODE, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<q.nranges, kThreads, L::SMEM, st>>>(ma, mb, a, q);
+  kern<<<q.nranges, kThreads + (PS ? 32 : 0), L::SMEM, st>>>(ma, mb, a, q);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -210,15 +230,24 @@ template <int MODE>
 cudaError_t agg_dispatch(const AggArgs &a, const View &va, const View &vb, const Queue &q, int dtype,
                          cudaStream_t st) {
   const bool bf = dtype == KDA_DTYPE_BF16;
+  if constexpr (MODE != 1) {
+    if (a.per_step) {
+      if (a.D == 64)
+        return bf ? agg_launch<__nv_bfloat16, 64, false, true, MODE>(a, va, vb, q, st)
+                  : agg_launch<__half, 64, false, true, MODE>(a, va, vb, q, st);
+      return bf ? agg_launch<__nv_bfloat16, 128, false, true, MODE>(a, va, vb, q, st)
+                : agg_launch<__half, 128, false, true, MODE>(a, va, vb, q, st);
+    }
+  }
   if (a.D == 64) {
     if (a.literal)
-      return bf ? agg_launch<__nv_bfloat16, 64, true, MODE>(a, va, vb, q, st)
-                : agg_launch<__half, 64, true, MODE>(a, va, vb, q, st);
-    return bf ? agg_launch<__nv_bfloat16, 64, false, MODE>(a, va, vb, q, st)
-              : agg_launch<__half, 64, false, MODE>(a, va, vb, q, st);
+      return bf ? agg_launch<__nv_bfloat16, 64, true, false, MODE>(a, va, vb, q, st)
+                : agg_launch<__half, 64, true, false, MODE>(a, va, vb, q, st);
+    return bf ? agg_launch<__nv_bfloat16, 64, false, false, MODE>(a, va, vb, q, st)
+              : agg_launch<__half, 64, false, false, MODE>(a, va, vb, q, st);
   }
-  return bf ? agg_launch<__nv_bfloat16, 128, false, MODE>(a, va, vb, q, st)
-            : agg_launch<__half, 128, false, MODE>(a, va, vb, q, st);
+  return bf ? agg_launch<__nv_bfloat16, 128, false, false, MODE>(a, va, vb, q, st)
+            : agg_launch<__half, 128, false, false, MODE>(a, va, vb, q, st);
 }
 
 }  // namespace

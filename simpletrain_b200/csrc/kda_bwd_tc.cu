@@ -18,10 +18,20 @@
 //   dv = K dS + P^T dO         (literal: dS^T K + P^T dO)
 //   dS <- decay^L dS + W
 //
+// Per-step decay (PS, one decay a per stream): q and k rows are scaled in
+// the stage by two extra warps, Q^ = diag(a^(i+1-kRef)) Q, K~ = diag(a^(kRef-1-j)) K,
+// and with them (m = kRef, L the chunk length)
+//   O  = tril(Q^ K~^T) V + Q^ (a^m S)         S <- a^L S + a^(L-m) K~^T V
+//   dq = diag(a^(i+1-m)) [tril(dO V^T) K~ + dO (a^m S)^T]
+//   dk = diag(a^(m-1-j)) [tril(dO V^T)^T Q^ + V (a^(L-m) dS)^T]
+//   dv = tril(Q^ K~^T)^T dO + K~ (a^(L-m) dS)  dS <- a^L dS + a^m Q^^T dO
+// i.e. the same products, scalar factors on the carries and a row factor on
+// dq and dk.  The decay is not differentiated in this mode.
+//
 // Warp 0: unit tickets + TMA loads (q, k, v, g, dy) into a two-stage ring;
 // warp 1: tensor memory and the single MMA-issuing thread; warps 2-9:
-// epilogue.  Outputs go straight from registers to global memory.  Every
-// wait is bounded.
+// epilogue (PS: warps 10-11 scale q and k).  Outputs leave through TMA
+// stores.  Every wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -40,6 +50,10 @@ using namespace tc;
 
 
 // forward-direction pass: stage = q, k, v, g, dy
+// threads of a backward CTA: + two row-scaler warps in per-step mode
+template <bool PS>
+constexpr int bwd_threads() { return kThreads + (PS ? 64 : 0); }
+
 template <int D, int NS>
 struct BwdLayout {
   static constexpr int KB = D / 64;
@@ -52,7 +66,7 @@ struct BwdLayout {
   static constexpr int PANEL = D * 128;  // [D rows x 64 columns] of the carried state operand
   static constexpr int SB = DO + BOX;
   static constexpr int BAR = SB + KB * PANEL;
-  static constexpr int NBAR = 2 * NS + 20;
+  static constexpr int NBAR = 3 * NS + 20;
   static constexpr int RING = BAR + NBAR * 8;
   static constexpr int RED = RING + 16;   // float [D] row sums
   static constexpr int TMEM_SLOT = RED + 4 * D;
@@ -77,7 +91,7 @@ struct RevLayout {
   static constexpr int DK = SB + KB * PANEL;
   static constexpr int DV = DK + BOX;
   static constexpr int BAR = DV + BOX;
-  static constexpr int NBAR = 2 * NS + 20;
+  static constexpr int NBAR = 3 * NS + 20;
   static constexpr int RING = BAR + NBAR * 8;
   static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
@@ -144,8 +158,8 @@ __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, ui
 // ===========================================================================
 // forward-direction pass: dq, dg, decay gradient
 // ===========================================================================
-template <typename T, int D, bool LIT, int NS>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int D, bool LIT, bool PS, int NS>
+__global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     bwd_fwddir_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
                          const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tdq,
@@ -161,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t A_DQ = L::A_QK;
   enum {
     QK_FULL = 2 * NS, DO_FULL, W_FULL, S_READY, KV_FULL, P_FULL, DP_FULL, DPM_FULL, O_FULL, DQ_FULL, OUT_FREE,
-    UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
+    UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -192,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(OUT_FREE), kEpi);  // O and dq were read
     mbar_init(bar(UNIT_FULL0), 1);
     mbar_init(bar(UNIT_FULL1), 1);
-    mbar_init(bar(UNIT_FREE0), 1 + kEpi);
-    mbar_init(bar(UNIT_FREE1), 1 + kEpi);
+    mbar_init(bar(UNIT_FREE0), 1 + kEpi + (PS ? 2 : 0));
+    mbar_init(bar(UNIT_FREE1), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(FIN), 1);
+    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -231,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
           // the last chunk's O and dq were read: A_QK, A_DP, A_X free
-          if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+          if (!(ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
                      mbar_wait(bar(OUT_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
@@ -293,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kThreads / 32) {
     const Epi e;
     Carry<D> Td;  // decay tangent (fp32 registers)
     Td.init_rows(e);
@@ -317,6 +332,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
       }
+      // per-step: carry factors a^kRef (operand of the first chunk), a^(64-kRef)
+      // (tensor-memory carry -> state), and the dq row factors a^(row+1-kRef)
+      float am = 1.f, au_f = 1.f, rq[2] = {1.f, 1.f};
+      if constexpr (PS) {
+        const float l2a = log2f(decay_value(a.decay, b, h, 0));
+        am = pow_log2(l2a, (float)kRef);
+        au_f = pow_log2(l2a, (float)(64 - kRef));
+        for (int ee = 0; ee < 2; ++ee) rq[ee] = pow_log2(l2a, (float)(e.r0 + 8 * ee + 1 - kRef));
+      }
       const bool early = u.early(qu);
       if (early) {
         // middle range: exit state and tangent follow from the entry ones and the aggregate:
@@ -334,6 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = (4 * i4) / Carry<D>::NV;
           const float4 sv = __ldcg(prev + i4 * kEpi + e.et);
           const float4 gs = __ldcg(ag + i4 * kEpi + e.et);
+          if constexpr (PS) {  // no tangent without a decay gradient
+            __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
+                                                       fmaf(A[r], sv.z, gs.z), fmaf(A[r], sv.w, gs.w)));
+            continue;
+          }
           const float4 gt = __ldcg(ag + (CF4 + i4) * kEpi + e.et);
           __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
                                                      fmaf(A[r], sv.z, gs.z), fmaf(A[r], sv.w, gs.w)));
@@ -395,6 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           float alr[Carry<D>::NR];
           for (int r = 0; r < Carry<D>::NR; ++r) alr[r] = (Lc == 64) ? af[r] : at[r];
           const float Lf = (float)Lc;
+          // factors of the loaded carry for the operand and for tensor memory; per-step:
+          // both a^kRef S_{c-1} (S_{c-1} = a^(64-kRef) Z from tensor memory past the first chunk)
+          float sop = 1.f, stm = alr[0];
+          if constexpr (PS) sop = stm = (c == u.c_begin) ? am : af[0];
           if (D == 128) {
             const int row = Td.row[0];
             constexpr int W = Carry<D>::W;
@@ -432,14 +465,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               for (int j = 0; j < 2; ++j)
                 st_shared_v4(pb + swz(row, (col0 & 63) + 8 * j),
-                             pack2(__uint_as_float(u32[8 * j]), __uint_as_float(u32[8 * j + 1]), BF),
-                             pack2(__uint_as_float(u32[8 * j + 2]), __uint_as_float(u32[8 * j + 3]), BF),
-                             pack2(__uint_as_float(u32[8 * j + 4]), __uint_as_float(u32[8 * j + 5]), BF),
-                             pack2(__uint_as_float(u32[8 * j + 6]), __uint_as_float(u32[8 * j + 7]), BF));
+                             pack2(sop * __uint_as_float(u32[8 * j]), sop * __uint_as_float(u32[8 * j + 1]), BF),
+                             pack2(sop * __uint_as_float(u32[8 * j + 2]), sop * __uint_as_float(u32[8 * j + 3]), BF),
+                             pack2(sop * __uint_as_float(u32[8 * j + 4]), sop * __uint_as_float(u32[8 * j + 5]), BF),
+                             pack2(sop * __uint_as_float(u32[8 * j + 6]), sop * __uint_as_float(u32[8 * j + 7]), BF));
               for (int k = 0; k < 16; ++k) {
                 const float sv = __uint_as_float(u32[k]);
-                Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
-                u32[k] = __float_as_uint(alr[0] * sv);
+                if constexpr (!PS) Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
+                u32[k] = __float_as_uint(stm * sv);
               }
               tmem_st_32x32b_x16_nowait(tmem + e.lane_off + L::A_Z + col0, u32);
             }
@@ -460,11 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int r = 0; r < Carry<D>::NR; ++r)
                 for (int k = 0; k < Carry<D>::NV; ++k) dl[r] = fmaf(Td.x[r][k], W.x[r][k], dl[r]);
             }
-            Sp.template write_operand<BF>(e, sb + L::SB);
+            Sp.template write_operand<BF>(e, sb + L::SB, sop);
             for (int r = 0; r < Carry<D>::NR; ++r)
               for (int k = 0; k < Carry<D>::NV; ++k) {
-                Td.x[r][k] = alr[r] * fmaf(Lf, Sp.x[r][k], Td.x[r][k]);
-                Sp.x[r][k] *= alr[r];
+                if constexpr (!PS) Td.x[r][k] = alr[r] * fmaf(Lf, Sp.x[r][k], Td.x[r][k]);
+                Sp.x[r][k] *= PS ? stm : alr[r];
               }
             Sp.tmem_store(e, tmem, L::A_Z);
           }
@@ -494,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (d) dq over the stage's gate tile (read only by the dO step), then a TMA store
         if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
         tc_fence_after();
-        frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false);
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false, rq);
         tc_fence_before();
         mbar_arrive(bar(OUT_FREE));
         fence_async_smem();
@@ -524,6 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           S.row[0] = Td.row[0];
           S.row[Carry<D>::NR - 1] = Td.row[Carry<D>::NR - 1];
           S.tmem_load(e, tmem, L::A_Z);
+          if constexpr (PS)  // tensor memory holds a^(kRef-64) S after a full chunk
+            for (int r = 0; r < Carry<D>::NR; ++r)
+              for (int k = 0; k < Carry<D>::NV; ++k) S.x[r][k] *= au_f;
           S.store_slot(e, slot);
           Td.store_slot(e, slot + CF4 * kEpi);
         }
@@ -552,6 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
       }
     }
+  } else if constexpr (PS) {
+    const bool is_q = warp == kThreads / 32;
+    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
+                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   if (threadIdx.x == 64) {
     tma_store_wait_all();  // dg / dq stores of the last chunk
@@ -567,8 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 // reverse pass: dk, dv, d(initial state)
 // ===========================================================================
-template <typename T, int D, bool LIT, int NS>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int D, bool LIT, bool PS, int NS>
+__global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     bwd_revdir_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                          const __grid_constant__ CUtensorMap tdk, const __grid_constant__ CUtensorMap tdv,
@@ -582,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // tensor memory: A_QK scores, A_DP dP, A_X dk, A_Y dv, A_Z W = Q^T dO
   enum {
     QK_FULL = 2 * NS, QK_FREE, DP_FULL, DP_FREE, W_FULL, W_FREE, DS_READY, DKV_FREE, INTER_FULL, P_FULL, DPM_FULL,
-    DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
+    DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -608,9 +648,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(DKV_FULL), 1);
     mbar_init(bar(UNIT_FULL0), 1);
     mbar_init(bar(UNIT_FULL1), 1);
-    mbar_init(bar(UNIT_FREE0), 1 + kEpi);
-    mbar_init(bar(UNIT_FREE1), 1 + kEpi);
+    mbar_init(bar(UNIT_FREE0), 1 + kEpi + (PS ? 2 : 0));
+    mbar_init(bar(UNIT_FREE1), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(FIN), 1);
+    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -644,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
-          if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+          if (!(ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
                      mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
@@ -706,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kThreads / 32) {
     const Epi e;
     Carry<D> dS;
     dS.init_rows(e);
@@ -724,6 +765,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         af[r] = chunk_alpha(a.decay, b, h, dS.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, dS.row[r], Ltail, 64);
       }
+      // per-step: W factor a^kRef, operand factor a^(L-kRef) for the chunk that
+      // reads it (full, or the stream's tail chunk first), dk row factors a^(kRef-1-row)
+      float am = 1.f, ad_f = 1.f, ad_0 = 1.f, rk[2] = {1.f, 1.f};
+      if constexpr (PS) {
+        const float l2a = log2f(decay_value(a.decay, b, h, 0));
+        const int L0 = min(64, a.T - 64 * (u.c_end - 1));
+        am = pow_log2(l2a, (float)kRef);
+        ad_f = pow_log2(l2a, (float)(64 - kRef));
+        ad_0 = pow_log2(l2a, (float)(L0 - kRef));
+        for (int ee = 0; ee < 2; ++ee) rk[ee] = pow_log2(l2a, (float)(kRef - 1 - e.r0 - 8 * ee));
+      }
       const bool early = u.early(qu);
       if (early) {
         // middle range: dS at its start follows from dS at its end and the aggregate
@@ -732,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         combine_store<D>(e, dS, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
         chain_publish(e, qu, u.pub_slot);
       }
-      dS.template write_operand<BF>(e, sb + L::SB);
+      dS.template write_operand<BF>(e, sb + L::SB, ad_0);
       fence_async_smem();
       named_bar_sync(1, kEpi);
       if (e.et == 0) mbar_arrive(bar(DS_READY));
@@ -774,20 +826,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t w32[32];
               tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_Z + Carry<D>::W * e.cg + 32 * sl, w32);
               for (int kk = 0; kk < 32; ++kk)
-                dS.x[0][32 * sl + kk] = fmaf(al[0], dS.x[0][32 * sl + kk], __uint_as_float(w32[kk]));
+                dS.x[0][32 * sl + kk] = fmaf(al[0], dS.x[0][32 * sl + kk], am * __uint_as_float(w32[kk]));
             }
           } else {
             Carry<D> W;
             W.tmem_load(e, tmem, L::A_Z);
             for (int r = 0; r < Carry<D>::NR; ++r)
-              for (int kk = 0; kk < Carry<D>::NV; ++kk) dS.x[r][kk] = fmaf(al[r], dS.x[r][kk], W.x[r][kk]);
+              for (int kk = 0; kk < Carry<D>::NV; ++kk) dS.x[r][kk] = fmaf(al[r], dS.x[r][kk], am * W.x[r][kk]);
           }
         }
         tc_fence_before();
         mbar_arrive(bar(W_FREE));
         if (e.et == 0) KDA_TRACE_EVENT(22, gc);
         if (k + 1 < u.c_end - u.c_begin) {
-          dS.template write_operand<BF>(e, sb + L::SB);
+          dS.template write_operand<BF>(e, sb + L::SB, ad_f);
           fence_async_smem();
           named_bar_sync(1, kEpi);
           if (e.et == 0) mbar_arrive(bar(DS_READY));
@@ -797,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(bar(DKV_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(24, gc);
         tc_fence_after();
-        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, sb + L::DK, 0, false);
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, sb + L::DK, 0, false, rk);
         if (e.et == 0) KDA_TRACE_EVENT(25, gc);
         frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_Y, sb + L::DV, 0, false);
         tc_fence_before();
@@ -824,6 +876,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (e.et == 0) tma_store_wait_all();
+  } else if constexpr (PS) {
+    const bool is_q = warp == kThreads / 32;
+    scaler_role<D, BF, NS>(qu, true, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
+                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   __syncthreads();
   if (warp == 1) {
@@ -832,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int D, bool LIT, int NS>
+template <typename T, int D, bool LIT, bool PS, int NS>
 cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, int grid1, int grid2,
                           cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
@@ -845,25 +901,25 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   if (!ok) return cudaErrorInvalidValue;
   using L1 = BwdLayout<D, NS>;
   using L2 = RevLayout<D, NS>;
-  auto k1 = bwd_fwddir_tc_kernel<T, D, LIT, NS>;
-  auto k2 = bwd_revdir_tc_kernel<T, D, LIT, NS>;
+  auto k1 = bwd_fwddir_tc_kernel<T, D, LIT, PS, NS>;
+  auto k2 = bwd_revdir_tc_kernel<T, D, LIT, PS, NS>;
   cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L1::SMEM);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L2::SMEM);
   if (e != cudaSuccess) return e;
   const int dtype = BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16;
-  if (q1.agg) {  // middle ranges: state and tangent aggregates from k, v
-    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q1.agg, q1.agg_f4, a.status};
-    if ((e = launch_agg_tc(1, g, a.k, a.v, q1, dtype, st)) != cudaSuccess) return e;
+  if (q1.agg) {  // middle ranges: state (and tangent) aggregates from k, v
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q1.agg, q1.agg_f4, a.status};
+    if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, st)) != cudaSuccess) return e;
   }
-  k1<<<grid1, kThreads, L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
+  k1<<<grid1, bwd_threads<PS>(), L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (q2.agg) {  // middle ranges: dS aggregates from q and the dO the first pass wrote
-    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q2.agg, q2.agg_f4, a.status};
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q2.agg, q2.agg_f4, a.status};
     if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, st)) != cudaSuccess) return e;
   }
-  k2<<<grid2, kThreads, L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
+  k2<<<grid2, bwd_threads<PS>(), L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -873,15 +929,22 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
 cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue &q2, int grid1, int grid2,
                           int dtype, cudaStream_t st) {
   const bool bf = dtype == KDA_DTYPE_BF16;
+  if (a.per_step) {
+    if (a.D == 64)
+      return bf ? bwd_tc_launch<__nv_bfloat16, 64, false, true, 2>(a, q1, q2, grid1, grid2, st)
+                : bwd_tc_launch<__half, 64, false, true, 2>(a, q1, q2, grid1, grid2, st);
+    return bf ? bwd_tc_launch<__nv_bfloat16, 128, false, true, 2>(a, q1, q2, grid1, grid2, st)
+              : bwd_tc_launch<__half, 128, false, true, 2>(a, q1, q2, grid1, grid2, st);
+  }
   if (a.D == 64) {
     if (a.literal)
-      return bf ? bwd_tc_launch<__nv_bfloat16, 64, true, 2>(a, q1, q2, grid1, grid2, st)
-                : bwd_tc_launch<__half, 64, true, 2>(a, q1, q2, grid1, grid2, st);
-    return bf ? bwd_tc_launch<__nv_bfloat16, 64, false, 2>(a, q1, q2, grid1, grid2, st)
-              : bwd_tc_launch<__half, 64, false, 2>(a, q1, q2, grid1, grid2, st);
+      return bf ? bwd_tc_launch<__nv_bfloat16, 64, true, false, 2>(a, q1, q2, grid1, grid2, st)
+                : bwd_tc_launch<__half, 64, true, false, 2>(a, q1, q2, grid1, grid2, st);
+    return bf ? bwd_tc_launch<__nv_bfloat16, 64, false, false, 2>(a, q1, q2, grid1, grid2, st)
+              : bwd_tc_launch<__half, 64, false, false, 2>(a, q1, q2, grid1, grid2, st);
   }
-  return bf ? bwd_tc_launch<__nv_bfloat16, 128, false, 2>(a, q1, q2, grid1, grid2, st)
-            : bwd_tc_launch<__half, 128, false, 2>(a, q1, q2, grid1, grid2, st);
+  return bf ? bwd_tc_launch<__nv_bfloat16, 128, false, false, 2>(a, q1, q2, grid1, grid2, st)
+            : bwd_tc_launch<__half, 128, false, false, 2>(a, q1, q2, grid1, grid2, st);
 }
 
 }  // namespace kda

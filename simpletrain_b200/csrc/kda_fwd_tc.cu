@@ -15,11 +15,16 @@
 //
 // Warp 0 takes range tickets (kda_tc_epi.cuh) and issues TMA loads of q, k, v
 // into an NS-stage ring; warp 1 owns tensor memory and one thread issues the
-// MMAs; warps 2-9 run the epilogue (two per TMEM sub-partition); warp 10
-// loads g into an NY-deep ring of tiles that the epilogue overwrites in place
-// with y = g * O and stores with TMA.  A piece starts from the initial state
+// MMAs; warps 2-9 run the epilogue (two per TMEM sub-partition); lane 1 of
+// warp 0 loads g into an NY-deep ring of tiles that the epilogue overwrites in
+// place with y = g * O and stores with TMA.  A piece starts from the initial state
 // or from the state published at its range boundary, and publishes its own
 // when it ends mid-stream.
+//
+// Per-step decay (PS): two more warps scale each stage's q and k rows in
+// place after the TMA load (kda_tc_epi.cuh, kRef); the MMAs wait for them,
+// the products are unchanged, and the epilogue applies the carry's scalar
+// factors: operand a^kRef S, S <- a^L S + a^(L-kRef) K~^T V.
 //
 // Pipelining: O is double-buffered in tensor memory and the epilogue runs
 // "state update of c -> store y_c -> mask P_{c+1}", so the MMAs of chunk c+1
@@ -59,7 +64,7 @@ struct FwdLayout {
   static constexpr int SB = P + kTile;  // S_{c-1}: KB panels of [D rows x 64]
   static constexpr int Y = SB + KB * D * 128;  // NY tiles (BOX each): g in, y out
   static constexpr int BAR = Y + NY * BOX;
-  static constexpr int NBAR = 2 * NS + 2 * NY + 16;
+  static constexpr int NBAR = 3 * NS + 2 * NY + 16;
   static constexpr int RING = BAR + NBAR * 8;  // two (ticket, piece) entries
   static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
@@ -68,8 +73,12 @@ struct FwdLayout {
   static constexpr uint32_t TMEM_COLS = (64 + 3 * D) <= 256 ? 256 : 512;
 };
 
-template <typename T, int D, bool LIT, int NS, int NY>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+// threads of a forward CTA: + two row-scaler warps in per-step mode
+template <bool PS>
+constexpr int fwd_threads() { return kFwdThreads + (PS ? 64 : 0); }
+
+template <typename T, int D, bool LIT, bool PS, int NS, int NY>
+__global__ void __launch_bounds__(fwd_threads<PS>(), 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
                   const __grid_constant__ CUtensorMap ty, const FwdArgs a, const Queue qu) {
@@ -82,7 +91,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
   enum {
     QK_FULL = 2 * NS + 2 * NY, QK_FREE, S_READY, O_FREE0, O_FREE1, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0,
-    UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN
+    UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
   };
   const int FULL = 0, EMPTY = NS, GFULL = 2 * NS, GEMPTY = 2 * NS + NY;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -112,9 +121,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(bar(QK_FULL + 8), 1);
     mbar_init(bar(QK_FULL + 9), 1);
     mbar_init(bar(QK_FULL + 10), 1);
-    mbar_init(bar(QK_FULL + 11), 2 + kEpi);  // unit ring slots: MMA, gate loader, epilogue
-    mbar_init(bar(QK_FULL + 12), 2 + kEpi);
+    mbar_init(bar(QK_FULL + 11), 2 + kEpi + (PS ? 2 : 0));  // unit ring slots: MMA, gate loader, epilogue, scalers
+    mbar_init(bar(QK_FULL + 12), 2 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(QK_FULL + 13), 1);
+    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -209,7 +219,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int c = u.c_begin; c < u.c_end && ok; ++c, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
-          ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag);
+          ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag);
           KDA_TRACE_EVENT(2, gc);
           ok = ok && mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag);
           if (!ok) break;
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_wait(bar(FIN), 0, a.status, abort_flag);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kFwdThreads / 32) {
     // ----------------------------------------------------------- epilogue
     const Epi e;
     Carry<D> S;
@@ -285,6 +295,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         af[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, S.row[r], Ltail, 64);
       }
+      // per-step: operand a^kRef S, U factor a^(L-kRef) (full / tail chunk)
+      float am = 1.f, au_f = 1.f, au_t = 1.f;
+      if constexpr (PS) {
+        const float l2a = log2f(decay_value(a.decay, b, h, 0));
+        am = pow_log2(l2a, (float)kRef);
+        au_f = pow_log2(l2a, (float)(64 - kRef));
+        au_t = pow_log2(l2a, (float)(Ltail - kRef));
+      }
       const bool early = u.early(qu);
       if (early) {
         // middle range: its exit state follows from the entry state and its aggregate
@@ -293,7 +311,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         combine_store<D>(e, S, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
         chain_publish(e, qu, u.pub_slot);
       }
-      S.template write_operand<BF>(e, sb + L::SB);
+      S.template write_operand<BF>(e, sb + L::SB, am);
       fence_async_smem();
       named_bar_sync(1, kEpi);
       if (e.et == 0) {
@@ -327,6 +345,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         {
           const bool upd = !(LIT && Lc != 64);
+          const float au = PS ? ((Lc == 64) ? au_f : au_t) : 1.f;
           if (D == 128) {
             const float al = (Lc == 64) ? af[0] : at[0];
             for (int sl = 0; sl < Carry<D>::NV / 32; ++sl) {
@@ -334,7 +353,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               tmem_ld_32x32b_x32(tmem + e.lane_off + L::A_KV + Carry<D>::W * e.cg + 32 * sl, uu);
               if (upd)
                 for (int k = 0; k < 32; ++k)
-                  S.x[0][32 * sl + k] = fmaf(al, S.x[0][32 * sl + k], __uint_as_float(uu[k]));
+                  S.x[0][32 * sl + k] = fmaf(al, S.x[0][32 * sl + k], au * __uint_as_float(uu[k]));
             }
           } else {
             Carry<D> U;
@@ -342,7 +361,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (upd)
               for (int r = 0; r < Carry<D>::NR; ++r) {
                 const float al = (Lc == 64) ? af[r] : at[r];
-                for (int k = 0; k < Carry<D>::NV; ++k) S.x[r][k] = fmaf(al, S.x[r][k], U.x[r][k]);
+                for (int k = 0; k < Carry<D>::NV; ++k) S.x[r][k] = fmaf(al, S.x[r][k], au * U.x[r][k]);
               }
           }
           tc_fence_before();
@@ -350,7 +369,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (e.et == 0) KDA_TRACE_EVENT(17, gc);
         }
         if (!last) {
-          S.template write_operand<BF>(e, sb + L::SB);
+          S.template write_operand<BF>(e, sb + L::SB, am);
           if (e.et == 0) KDA_TRACE_EVENT(18, gc);
           fence_async_smem();
           if (e.et == 0) KDA_TRACE_EVENT(19, gc);
@@ -431,6 +450,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       KDA_TRACE_CTA(2, kda_globaltimer());
       KDA_TRACE_CTA(3, gc);
     }
+  } else if constexpr (PS) {
+    // ------------------------------------------------------- row scalers
+    const bool is_q = warp == kFwdThreads / 32;
+    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
+                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   __syncthreads();
   if (warp == 1) {
@@ -439,7 +463,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-template <typename T, int D, bool LIT, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
+template <typename T, int D, bool LIT, bool PS, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
 cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mg, my;
@@ -449,27 +473,28 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
       !make_tmap_bhtd(&my, a.y, a.B, a.H, a.T, a.D, BF))
     return cudaErrorInvalidValue;
   using L = FwdLayout<D, NS, NY>;
-  auto kern = fwd_tc_kernel<T, D, LIT, NS, NY>;
+  auto kern = fwd_tc_kernel<T, D, LIT, PS, NS, NY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
   if (q.agg) {  // middle ranges: their state aggregates first
-    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.decay, q.agg, q.agg_f4, a.status};
+    const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q.agg, q.agg_f4, a.status};
     e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, st);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, kFwdThreads, L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
+  kern<<<grid, fwd_threads<PS>(), L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
   count_launches(1);
   return cudaGetLastError();
 }
 
-template <typename T, int D, bool LIT, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
+template <typename T, int D, bool LIT, bool PS, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
 int fwd_ctas_per_sm() {
-  auto kern = fwd_tc_kernel<T, D, LIT, NS, NY>;
+  auto kern = fwd_tc_kernel<T, D, LIT, PS, NS, NY>;
   int n = 0;
   // the dynamic shared memory must be allowed before the occupancy query counts it
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<D, NS, NY>::SMEM) !=
           cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kFwdThreads, FwdLayout<D, NS, NY>::SMEM) != cudaSuccess)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, fwd_threads<PS>(), FwdLayout<D, NS, NY>::SMEM) !=
+          cudaSuccess)
     return 1;
   // tensor memory is not in the occupancy model: a CTA holds TMEM_COLS of the SM's 512 columns
   const int tmem_cap = 512 / (int)FwdLayout<D, NS, NY>::TMEM_COLS;
@@ -479,23 +504,37 @@ int fwd_ctas_per_sm() {
 
 }  // namespace
 
-int fwd_tc_occupancy(int D, int dtype, bool literal) {
+int fwd_tc_occupancy(int D, int dtype, bool literal, bool per_step) {
   const bool bf = dtype == KDA_DTYPE_BF16;
-  if (D == 64) {
-    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true>() : fwd_ctas_per_sm<__half, 64, true>();
-    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false>() : fwd_ctas_per_sm<__half, 64, false>();
+  if (per_step) {
+    if (D == 64) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, true>() : fwd_ctas_per_sm<__half, 64, false, true>();
+    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, true>() : fwd_ctas_per_sm<__half, 128, false, true>();
   }
-  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false>() : fwd_ctas_per_sm<__half, 128, false>();
+  if (D == 64) {
+    if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true, false>() : fwd_ctas_per_sm<__half, 64, true, false>();
+    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, false>() : fwd_ctas_per_sm<__half, 64, false, false>();
+  }
+  return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, false>() : fwd_ctas_per_sm<__half, 128, false, false>();
 }
 
 cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dtype, cudaStream_t st) {
   const bool bf = dtype == KDA_DTYPE_BF16;
+  if (a.per_step) {
+    if (a.D == 64)
+      return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, true>(a, q, grid, st)
+                : fwd_tc_launch<__half, 64, false, true>(a, q, grid, st);
+    return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, true>(a, q, grid, st)
+              : fwd_tc_launch<__half, 128, false, true>(a, q, grid, st);
+  }
   if (a.D == 64) {
     if (a.literal)
-      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true>(a, q, grid, st) : fwd_tc_launch<__half, 64, true>(a, q, grid, st);
-    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false>(a, q, grid, st) : fwd_tc_launch<__half, 64, false>(a, q, grid, st);
+      return bf ? fwd_tc_launch<__nv_bfloat16, 64, true, false>(a, q, grid, st)
+                : fwd_tc_launch<__half, 64, true, false>(a, q, grid, st);
+    return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, false>(a, q, grid, st)
+              : fwd_tc_launch<__half, 64, false, false>(a, q, grid, st);
   }
-  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false>(a, q, grid, st) : fwd_tc_launch<__half, 128, false>(a, q, grid, st);
+  return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, false>(a, q, grid, st)
+            : fwd_tc_launch<__half, 128, false, false>(a, q, grid, st);
 }
 
 }  // namespace kda

@@ -28,6 +28,7 @@ struct DecaySrc {
 struct FwdArgs {
   int B, H, T, D, C;
   int literal;
+  int per_step;  // per-token decay (s_t = a s_{t-1} + k_t^T v_t), one decay per stream
   View q, k, v, g, y;  // g.data == nullptr -> no gate
   DecaySrc decay;
   const float *s_in;
@@ -38,6 +39,7 @@ struct FwdArgs {
 struct BwdArgs {
   int B, H, T, D, C;
   int literal;
+  int per_step;
   View q, k, v, g, dy, dq, dk, dv, dg;
   View dO;  // workspace [B][H][T][D] 16-bit: dy * g, written by the forward-direction pass
   DecaySrc decay;
@@ -72,6 +74,7 @@ struct Queue;
 struct AggArgs {
   int B, H, T, D;
   int literal;
+  int per_step;
   DecaySrc decay;
   float4 *agg;
   int agg_f4;
@@ -84,9 +87,10 @@ cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dt
 cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue &q2, int grid1, int grid2,
                           int dtype, cudaStream_t st);
 // mode 0: S from (k, v); 1: S and decay tangent from (k, v); 2: dS from (q, dO).
+// a.per_step takes modes 0 and 2.
 cudaError_t launch_agg_tc(int mode, const AggArgs &a, const View &va, const View &vb, const tc::Queue &q, int dtype,
                           cudaStream_t st);
 // CTAs of the forward kernel that fit on one SM.
-int fwd_tc_occupancy(int D, int dtype, bool literal);
+int fwd_tc_occupancy(int D, int dtype, bool literal, bool per_step);
 
 }  // namespace kda

@@ -209,18 +209,20 @@ struct Carry {
       else tmem_st_16x256b_x4(tmem + e.lane_off + acc + W * e.cg, u);
     }
   }
-  // 16-bit copy into a state operand (panels of [D rows x 64 cols])
+  // 16-bit copy of sc * carry into a state operand (panels of [D rows x 64 cols])
   template <bool BF>
-  __device__ void write_operand(const Epi &e, uint32_t base) const {
+  __device__ __forceinline__ void write_operand(const Epi &e, uint32_t base, float sc = 1.f) const {
     if constexpr (D == 128) {
-      for (int j = 0; j < W / 8; ++j)
-        st_shared_v4(panel_addr<D>(base, row[0], W * e.cg + 8 * j), pack2(x[0][8 * j], x[0][8 * j + 1], BF),
-                     pack2(x[0][8 * j + 2], x[0][8 * j + 3], BF), pack2(x[0][8 * j + 4], x[0][8 * j + 5], BF),
-                     pack2(x[0][8 * j + 6], x[0][8 * j + 7], BF));
+      for (int j = 0; j < W / 8; ++j) {
+        const float *f = &x[0][8 * j];
+        st_shared_v4(panel_addr<D>(base, row[0], W * e.cg + 8 * j), pack2(sc * f[0], sc * f[1], BF),
+                     pack2(sc * f[2], sc * f[3], BF), pack2(sc * f[4], sc * f[5], BF), pack2(sc * f[6], sc * f[7], BF));
+      }
     } else {
       for (int r = 0; r < NR; ++r)
         for (int j = 0; j < W / 8; ++j)
-          st_shared_u32(panel_addr<D>(base, row[r], W * e.cg + 8 * j + e.cq), pack2(x[r][2 * j], x[r][2 * j + 1], BF));
+          st_shared_u32(panel_addr<D>(base, row[r], W * e.cg + 8 * j + e.cq),
+                        pack2(sc * x[r][2 * j], sc * x[r][2 * j + 1], BF));
     }
   }
 };
@@ -276,11 +278,12 @@ __device__ void masked_tile(const Epi &e, uint32_t taddr, uint32_t dst) {
 
 // M=64 accumulator of D columns at `taddr` -> 16-bit tile at `tile` (KB boxes),
 // each value optionally scaled by the 16-bit tile `scale` at the same place
-// (which may be `tile` itself).  Loads go first: the shared-memory accesses are
+// (which may be `tile` itself) and by a factor per row (rs[0] for row r0,
+// rs[1] for row r0 + 8).  Loads go first: the shared-memory accesses are
 // ordered asm.
 template <int D, bool BF>
 __device__ __forceinline__ void frag_to_tile(const Epi &e, uint32_t taddr, uint32_t tile, uint32_t scale,
-                                             bool scaled) {
+                                             bool scaled, const float (&rs)[2] = {1.f, 1.f}) {
   constexpr int W = D / kQ;
   Frag<W> f;
   ld_frag(taddr + W * e.cg, f);
@@ -290,13 +293,47 @@ __device__ __forceinline__ void frag_to_tile(const Epi &e, uint32_t taddr, uint3
       for (int ee = 0; ee < 2; ++ee) sv[2 * j + ee] = ld_shared_u32(box_addr(scale, e.r0 + 8 * ee, W * e.cg + 8 * j + e.cq));
   for (int j = 0; j < W / 8; ++j)
     for (int ee = 0; ee < 2; ++ee) {
-      float v0 = f.v(ee, j, 0), v1 = f.v(ee, j, 1);
+      float v0 = rs[ee] * f.v(ee, j, 0), v1 = rs[ee] * f.v(ee, j, 1);
       if (scaled) {
         const float2 s2 = unpack2(sv[2 * j + ee], BF);
         v0 *= s2.x;
         v1 *= s2.y;
       }
       st_shared_u32(box_addr(tile, e.r0 + 8 * ee, W * e.cg + 8 * j + e.cq), pack2(v0, v1, BF));
+    }
+}
+
+// ------------------------------------------------------ per-step decay --
+// Per-step semantics (one decay a per stream, s_t = a s_{t-1} + k_t^T v_t)
+// run on the chunk kernels with row-scaled q and k tiles
+//   Q^ = diag(a^(i+1-kRef)) Q,   K~ = diag(a^(kRef-1-j)) K,
+// so that q^_i . k~_j = a^(i-j) q_i . k_j and every factor stays within
+// [a^kRef, a^-kRef]; the carried state picks up scalar factors only.
+constexpr int kRef = 32;
+
+// a^e for the per-step decay of a stream (log2 a given)
+__device__ __forceinline__ float pow_log2(float l2a, float e) { return exp2f(l2a * e); }
+
+// Scales rows `lane` and `lane + 32` of a [64 x 64 KB] 16-bit tile (KB
+// swizzled boxes) in place by f0 and f1.  A row is one 128-byte line of each
+// box whatever the swizzle, so a row factor needs no column mapping; each lane
+// starts at a different 16-byte chunk so that a warp's accesses cover all banks.
+template <int KB, bool BF>
+__device__ __forceinline__ void scale_tile_rows(uint32_t tile, int lane, float f0, float f1) {
+  for (int kb = 0; kb < KB; ++kb)
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint32_t line = tile + (uint32_t)(kb * kTile) + (uint32_t)((lane + 32 * hh) * 128);
+      const float f = hh ? f1 : f0;
+      uint4 v[8];
+      for (int c = 0; c < 8; ++c) v[c] = ld_shared_v4(line + (((c + lane) & 7) << 4));
+      for (int c = 0; c < 8; ++c) {
+        uint32_t *pv = &v[c].x;
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = unpack2(pv[k], BF);
+          pv[k] = pack2(f * x.x, f * x.y, BF);
+        }
+        st_shared_v4(line + (((c + lane) & 7) << 4), v[c].x, v[c].y, v[c].z, v[c].w);
+      }
     }
 }
 
@@ -421,6 +458,43 @@ __device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, c
     const float4 g = __ldcg(agg + i4 * kEpi + e.et);
     __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(a, f[4 * i4], g.x), fmaf(a, f[4 * i4 + 1], g.y),
                                                fmaf(a, f[4 * i4 + 2], g.z), fmaf(a, f[4 * i4 + 3], g.w)));
+  }
+}
+
+// Per-step mode: one warp scales the q (is_q) or the k tile of every stage
+// after its TMA load and before its MMAs (which wait on `SCALED + stage`,
+// one arrival per scaler warp).  Units come from the same two-entry ring as
+// the other roles; each warp frees a ring entry with one arrival.
+template <int D, bool BF, int NS>
+__device__ void scaler_role(const Queue &qu, bool reverse, int H, const DecaySrc &dec, uint32_t sb,
+                            int stage_bytes, uint32_t tile_off, bool is_q, volatile int *ring,
+                            volatile int *abort_flag, int32_t *status, uint32_t bar_base, int FULL, int SCALED,
+                            int UNIT_FULL0, int UNIT_FREE0) {
+  const int lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return bar_base + 8u * i; };
+  int gc = 0;
+  for (int i = 0;; ++i) {
+    // every lane waits; the warp leaves together if any lane's wait gave up
+    if (!__all_sync(0xffffffffu, mbar_wait(bar(UNIT_FULL0 + (i & 1)), (i >> 1) & 1, status, abort_flag))) break;
+    const int t = ring[2 * (i & 1)], p = ring[2 * (i & 1) + 1];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(UNIT_FREE0 + (i & 1)));
+    if (t >= qu.nranges) break;
+    const Piece u = piece_of(qu, span_of(qu, t, reverse), p, reverse);
+    const int b = u.stream / H, h = u.stream - b * H;
+    const float l2a = log2f(decay_value(dec, b, h, 0));
+    const float e0 = is_q ? (float)(lane + 1 - kRef) : (float)(kRef - 1 - lane);
+    const float f0 = pow_log2(l2a, e0), f1 = pow_log2(l2a, is_q ? e0 + 32.f : e0 - 32.f);
+    bool ok = true;
+    for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
+      const int s = gc % NS, use = gc / NS;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(FULL + s), use & 1, status, abort_flag)))) break;
+      scale_tile_rows<D / 64, BF>(sb + (uint32_t)(s * stage_bytes) + tile_off, lane, f0, f1);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(SCALED + s));
+    }
+    if (!ok) break;
   }
 }
 

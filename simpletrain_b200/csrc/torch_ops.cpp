@@ -92,6 +92,13 @@ void decay_fields(const optional<Tensor> &decay, const float **p, int64_t *sb, i
   *sd = d.size(2) == 1 ? 0 : d.stride(2);
 }
 
+// state-update semantics of the ops: 0 = K^T V (chunk-constant decay), 1 = the
+// reference's literal K V^T, 2 = per-token decay
+uint32_t mode_flags(int64_t mode) {
+  TORCH_CHECK(mode >= 0 && mode <= 2, "mode must be 0 (corrected), 1 (literal) or 2 (per-step), got ", mode);
+  return mode == 1 ? KDA_FLAG_LITERAL : (mode == 2 ? KDA_FLAG_PER_STEP : 0u);
+}
+
 void check(int rc, const char *what) {
   TORCH_CHECK(rc == KDA_OK, what, " failed: ", kda_status_string(rc), " (status ", rc, ")");
 }
@@ -111,7 +118,7 @@ void check_inputs(const Tensor &q, const Tensor &k, const Tensor &v, const optio
 
 std::tuple<Tensor, Tensor> chunk_fwd(const Tensor &q_, const Tensor &k_, const Tensor &v_,
                                      const optional<Tensor> &g_, const optional<Tensor> &decay,
-                                     double decay_scalar, const optional<Tensor> &s0, int64_t chunk, bool literal,
+                                     double decay_scalar, const optional<Tensor> &s0, int64_t chunk, int64_t mode,
                                      bool want_state) {
   check_inputs(q_, k_, v_, g_);
   c10::cuda::CUDAGuard guard(q_.device());
@@ -122,7 +129,7 @@ std::tuple<Tensor, Tensor> chunk_fwd(const Tensor &q_, const Tensor &k_, const T
   const auto f32 = q.options().dtype(at::kFloat);
   const Tensor s_out = want_state ? at::empty({B, H, D, D}, f32) : at::empty({0}, f32);
   const optional<Tensor> s_in = s0.has_value() ? optional<Tensor>(s0->contiguous().to(at::kFloat)) : c10::nullopt;
-  const uint32_t flags = literal ? KDA_FLAG_LITERAL : 0u;
+  const uint32_t flags = mode_flags(mode);
   const size_t ws_bytes = kda_fwd_workspace_bytes((int32_t)B, (int32_t)H, (int32_t)T, (int32_t)D, (int32_t)chunk, flags);
   const Tensor ws = at::empty({(int64_t)ws_bytes}, q.options().dtype(at::kByte));
   kda_fwd_params p{};
@@ -144,7 +151,7 @@ std::tuple<Tensor, Tensor> chunk_fwd(const Tensor &q_, const Tensor &k_, const T
 std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> chunk_bwd(
     const Tensor &q_, const Tensor &k_, const Tensor &v_, const optional<Tensor> &g_, const Tensor &dy_,
     const optional<Tensor> &decay, double decay_scalar, const optional<Tensor> &s0, const optional<Tensor> &s_T,
-    const optional<Tensor> &ds_T, int64_t chunk, bool literal, bool need_ddecay_, bool need_ds0) {
+    const optional<Tensor> &ds_T, int64_t chunk, int64_t mode, bool need_ddecay_, bool need_ds0) {
   (void)s_T;
   check_inputs(q_, k_, v_, g_);
   c10::cuda::CUDAGuard guard(q_.device());
@@ -161,7 +168,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> chunk_bwd(
   const optional<Tensor> dsT = (ds_T.has_value() && ds_T->numel() > 0)
                                    ? optional<Tensor>(ds_T->contiguous().to(at::kFloat))
                                    : c10::nullopt;
-  const uint32_t flags = literal ? KDA_FLAG_LITERAL : 0u;
+  const uint32_t flags = mode_flags(mode);
   const size_t ws_bytes = kda_bwd_workspace_bytes((int32_t)B, (int32_t)H, (int32_t)T, (int32_t)D, (int32_t)chunk, flags);
   const Tensor ws = at::empty({(int64_t)ws_bytes}, q.options().dtype(at::kByte));
   kda_bwd_params p{};
@@ -294,10 +301,10 @@ TORCH_LIBRARY_IMPL(st_b200, CUDA, m) {
 TORCH_LIBRARY(kda_b200, m) {
   m.def(
       "chunk_fwd(Tensor q, Tensor k, Tensor v, Tensor? g, Tensor? decay, float decay_scalar, Tensor? s0, "
-      "int chunk, bool literal, bool want_state) -> (Tensor, Tensor)");
+      "int chunk, int mode, bool want_state) -> (Tensor, Tensor)");
   m.def(
       "chunk_bwd(Tensor q, Tensor k, Tensor v, Tensor? g, Tensor dy, Tensor? decay, float decay_scalar, "
-      "Tensor? s0, Tensor? s_T, Tensor? ds_T, int chunk, bool literal, bool need_ddecay, bool need_ds0) "
+      "Tensor? s0, Tensor? s_T, Tensor? ds_T, int chunk, int mode, bool need_ddecay, bool need_ds0) "
       "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
   m.def("status_word(int device) -> Tensor");
 }

@@ -26,6 +26,9 @@ variable ``KDA_B200_SEMANTICS`` read at import):
 * ``"literal"`` -- always the reference's update; raises like the reference
   (``RuntimeError``, same message) when D != chunk_size.
 * ``"corrected"`` -- always ``K^T V``.
+* ``"per_step"`` -- the per-token recurrence of the reference's docstring
+  (``:8-11``) and Triton kernel (``:134-180``), ``s_t = decay s_{t-1} +
+  k_t^T v_t``, with one decay per (batch, head) in [0.125, 1].
 
 Errors: non-fp16/bf16 inputs raise ``AssertionError`` (the reference's
 Triton wrapper asserts the same, ``:204``); CPU tensors raise
@@ -62,11 +65,18 @@ def _use_literal(D: int, T: int, chunk_size: int) -> bool:
     mode = SEMANTICS
     if mode == "literal":
         return True
-    if mode == "corrected":
+    if mode in ("corrected", "per_step"):
         return False
     if mode != "auto":
-        raise ValueError(f"SEMANTICS must be 'auto', 'literal' or 'corrected', got {mode!r}")
+        raise ValueError(f"SEMANTICS must be 'auto', 'literal', 'corrected' or 'per_step', got {mode!r}")
     return D == chunk_size and (T % chunk_size) in (0, 1)
+
+
+def _per_step_decay_arg(decay: Union[float, torch.Tensor], B: int, H: int):
+    """A float, or a tensor broadcasting as [B, H, 1, 1] (one decay per head), as [B, H, 1]."""
+    if not torch.is_tensor(decay):
+        return float(decay)
+    return torch.broadcast_to(decay.float(), (B, H, 1, 1)).reshape(B, H, 1)
 
 
 def _decay_arg(decay: Union[float, torch.Tensor], B: int, H: int, D: int):
@@ -90,6 +100,10 @@ def kda_chunked_scan_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise AssertionError("KDA sm_100a kernel requires fp16/bf16")
     _validate(q, k, v, gate, chunk_size)
     B, H, T, D = q.shape
+    if SEMANTICS == "per_step":
+        y, _ = kda_chunk(q, k, v, gate, _per_step_decay_arg(decay, B, H), None, chunk_size,
+                         output_final_state=False, per_step=True)
+        return y
     literal = _use_literal(D, T, chunk_size)
     y, _ = kda_chunk(q, k, v, gate, _decay_arg(decay, B, H, D), None, chunk_size,
                      reference_exact=literal, output_final_state=False)

@@ -106,15 +106,19 @@ def _validate(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], chunk: int):
 # --------------------------------------------------------------------------- #
 # fake implementations (shapes only) for tracing
 # --------------------------------------------------------------------------- #
+# state-update semantics passed to the ops
+MODE_CORRECTED, MODE_LITERAL, MODE_PER_STEP = 0, 1, 2
+
+
 @torch.library.register_fake("kda_b200::chunk_fwd")
-def _(q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state):
+def _(q, k, v, g, decay, decay_scalar, s0, chunk, mode, want_state):
     B, H, T, D = q.shape
     shape = (B, H, D, D) if want_state else (0,)
     return torch.empty_like(q), q.new_empty(shape, dtype=torch.float32)
 
 
 @torch.library.register_fake("kda_b200::chunk_bwd")
-def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, literal, need_ddecay, need_ds0):
+def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, mode, need_ddecay, need_ds0):
     B, H, T, D = q.shape
     f32 = torch.float32
     dg = torch.empty_like(g) if g is not None else q.new_empty((0,))
@@ -127,12 +131,12 @@ def _(q, k, v, g, dy, decay, decay_scalar, s0, s_T, ds_T, chunk, literal, need_d
 # autograd
 # --------------------------------------------------------------------------- #
 def _setup_context(ctx, inputs, output):
-    q, k, v, g, decay, decay_scalar, s0, chunk, literal, want_state = inputs
+    q, k, v, g, decay, decay_scalar, s0, chunk, mode, want_state = inputs
     y, s_T = output
     ctx.save_for_backward(q, k, v, g, decay, s0, s_T if want_state else None)
     ctx.decay_scalar = decay_scalar
     ctx.chunk = chunk
-    ctx.literal = literal
+    ctx.mode = mode
     ctx.has_gate = g is not None
 
 
@@ -140,6 +144,8 @@ def _backward(ctx, dy, ds_T):
     q, k, v, g, decay, s0, s_T = ctx.saved_tensors
     need = ctx.needs_input_grad
     need_ddecay = bool(need[4]) and decay is not None
+    if need_ddecay and ctx.mode == MODE_PER_STEP:
+        raise NotImplementedError("per-step mode does not differentiate the decay")
     need_ds0 = bool(need[6]) and s0 is not None
     if dy is None:
         dy = torch.zeros_like(q)
@@ -147,7 +153,7 @@ def _backward(ctx, dy, ds_T):
     dq, dk, dv, dg, ddecay, ds0 = torch.ops.kda_b200.chunk_bwd(
         q, k, v, g, dy, decay, ctx.decay_scalar, s0,
         s_T if use_dsT else None, ds_T if use_dsT else None,
-        ctx.chunk, ctx.literal, need_ddecay, need_ds0)
+        ctx.chunk, ctx.mode, need_ddecay, need_ds0)
     return (dq, dk, dv, dg if ctx.has_gate else None,
             ddecay if need_ddecay else None, None,
             ds0 if need_ds0 else None, None, None, None)
@@ -173,10 +179,31 @@ def decay_as_bhd(decay: Union[float, Tensor], B: int, H: int, D: int) -> Tuple[O
     return torch.broadcast_to(d, (B, H, D)), 0.0
 
 
+def per_step_decay(decay: Union[float, Tensor], B: int, H: int, D: int) -> Tuple[Optional[Tensor], float]:
+    """Per-step decay as (fp32 [B,H,D] view constant along D, or None, scalar).
+
+    Accepted: a float in [0.125, 1], or a tensor of shape (), (H,) (per head)
+    or anything broadcastable to (B, H, 1) (one decay per batch and head).
+    """
+    if not torch.is_tensor(decay):
+        a = float(decay)
+        if not 0.125 <= a <= 1.0:
+            raise ValueError(f"per-step decay must lie in [0.125, 1], got {a}")
+        return None, a
+    if decay.requires_grad:
+        raise NotImplementedError("per-step mode does not differentiate the decay")
+    d = decay.float()
+    if d.dim() == 1 and d.shape[0] == H:
+        d = d.view(H, 1)
+    if d.dim() >= 1 and d.shape[-1] != 1:
+        raise ValueError("per-step decay is one value per (batch, head): its last dimension must be 1")
+    return torch.broadcast_to(d, (B, H, 1)).expand(B, H, D), 0.0
+
+
 def kda_chunk(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
               decay: Union[float, Tensor] = 0.99, initial_state: Optional[Tensor] = None,
               chunk_size: int = 64, reference_exact: bool = False,
-              output_final_state: bool = True) -> Tuple[Tensor, Optional[Tensor]]:
+              output_final_state: bool = True, per_step: bool = False) -> Tuple[Tensor, Optional[Tensor]]:
     """KDA chunked scan on B200: returns ``(y, final_state)``.
 
     q, k, v, g: ``[B, H, T, D]`` bf16/fp16 CUDA tensors (any strides; the
@@ -187,18 +214,27 @@ def kda_chunk(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
     reference's literal ``K V^T`` state update (``kernels/kda_kernel.py:294``,
     needs D == chunk_size); the default is the ``K^T V`` form.  Differentiable
     in q, k, v, g, a tensor decay and the initial state.
+
+    ``per_step`` selects the per-token recurrence of the reference's docstring
+    (``kernels/kda_kernel.py:8-11``): ``s_t = a s_{t-1} + k_t^T v_t``,
+    ``y_t = g_t * (q_t s_t)``, with one decay per (batch, head) (see
+    ``per_step_decay``); the final state is ``s_T``.  Differentiable in q, k, v,
+    g and the initial state (not the decay).
     """
     _validate(q, k, v, g, chunk_size)
     B, H, T, D = q.shape
+    if per_step and reference_exact:
+        raise ValueError("per_step and reference_exact are different semantics; pick one")
     if reference_exact and D != chunk_size:
         raise RuntimeError(
             f"The size of tensor a ({D}) must match the size of tensor b ({chunk_size}) "
             f"at non-singleton dimension 3")
     if reference_exact and output_final_state and T % chunk_size:
         raise ValueError("reference_exact: the final state of a ragged last chunk is not defined")
-    dt, ds = decay_as_bhd(decay, B, H, D)
+    dt, ds = per_step_decay(decay, B, H, D) if per_step else decay_as_bhd(decay, B, H, D)
     if initial_state is not None and initial_state.shape != (B, H, D, D):
         raise ValueError(f"initial_state must be [B, H, D, D] = {(B, H, D, D)}")
+    mode = MODE_PER_STEP if per_step else (MODE_LITERAL if reference_exact else MODE_CORRECTED)
     y, s = torch.ops.kda_b200.chunk_fwd(q, k, v, g, dt, ds, initial_state, int(chunk_size),
-                                        bool(reference_exact), bool(output_final_state))
+                                        mode, bool(output_final_state))
     return y, (s if output_final_state else None)

@@ -98,6 +98,32 @@ def test_forward_argument_checks(kw, code):
     assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params(**kw)), None) == code
 
 
+def _bwd_params(**kw):
+    p = _ffi.KdaBwdParams()
+    p.B, p.H, p.T, p.D, p.chunk, p.dtype = 1, 1, 64, 64, 64, _ffi.KDA_DTYPE_BF16
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize("kw", [
+    dict(flags=_ffi.KDA_FLAG_PER_STEP | _ffi.KDA_FLAG_LITERAL),            # two semantics at once
+    dict(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=0.1),                   # below the row-scaling range
+    dict(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=1.5),
+    dict(flags=_ffi.KDA_FLAG_PER_STEP, decay=0x10000, decay_stride_d=1),    # varies along the key channels
+])
+def test_per_step_argument_checks(kw):
+    lib = _ffi.load()
+    assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params(**kw)), None) == _ffi.KDA_ERR_UNSUPPORTED
+    assert lib.kda_bwd_sm100(ctypes.byref(_bwd_params(**kw)), None) == _ffi.KDA_ERR_UNSUPPORTED
+
+
+def test_per_step_backward_has_no_decay_gradient():
+    lib = _ffi.load()
+    p = _bwd_params(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=0.9, ddecay=0x10000)
+    assert lib.kda_bwd_sm100(ctypes.byref(p), None) == _ffi.KDA_ERR_UNSUPPORTED
+
+
 def test_null_params_and_missing_tensors():
     lib = _ffi.load()
     assert lib.kda_fwd_sm100(None, None) == _ffi.KDA_ERR_NULL_ARGUMENT

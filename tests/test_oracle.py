@@ -201,3 +201,51 @@ def test_seeded_workloads_shapes_and_layout():
     assert inp["decay"].shape == (3, 64) and inp["s0"] is None
     w4 = WORKLOADS["10b-fwdbwd"]
     assert w4.s0_std == 0.02 and w4.decay_mean == 4.0
+
+
+# --------------------------------------------------------------------------- #
+# per-step (docstring) semantics: the chunked restatement the kernels run
+# --------------------------------------------------------------------------- #
+@pytest.mark.parametrize("B,H,T,D,decay,gate,with_s0", [
+    (1, 2, 150, 8, 0.9, True, True),       # ragged last chunk
+    (2, 1, 64, 16, 0.5, False, False),
+    (1, 2, 200, 8, 0.125, True, True),     # smallest supported decay
+    (1, 1, 129, 8, 1.0, True, False),
+    (1, 3, 70, 4, "head", True, True),     # one decay per head
+])
+def test_per_step_chunked_form_and_backward_match_the_recurrence(B, H, T, D, decay, gate, with_s0):
+    from oracle.kda_oracle import per_step_chunk_scan, per_step_manual_backward, per_step_recurrence
+    g = torch.Generator().manual_seed(21)
+    q, k, v, gt = (torch.randn(B, H, T, D, generator=g, dtype=torch.float64) for _ in range(4))
+    gt = gt if gate else None
+    dec = torch.tensor([0.9, 0.5, 0.99], dtype=torch.float64) if decay == "head" else decay
+    s0 = torch.randn(B, H, D, D, generator=g, dtype=torch.float64) if with_s0 else None
+    y1, s1 = per_step_recurrence(q, k, v, gt, dec, s0)
+    y2, s2 = per_step_chunk_scan(q, k, v, gt, dec, 64, s0)
+    assert max_rel(y2, y1) < 1e-12 and max_rel(s2, s1) < 1e-12
+    leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+    gl = gt.clone().requires_grad_() if gt is not None else None
+    sl = s0.clone().requires_grad_() if s0 is not None else None
+    y, s = per_step_recurrence(*leaves, gl, dec, sl)
+    dy, dsT = torch.randn_like(y), torch.randn_like(s)
+    ((y * dy).sum() + (s * dsT).sum()).backward()
+    dq, dk, dv, dg, ds0 = per_step_manual_backward(q, k, v, gt, dec, 64, s0, dy, dsT)
+    pairs = [(dq, leaves[0].grad), (dk, leaves[1].grad), (dv, leaves[2].grad)]
+    if gl is not None:
+        pairs.append((dg, gl.grad))
+    if sl is not None:
+        pairs.append((ds0, sl.grad))
+    for got, ref in pairs:
+        assert max_rel(got, ref) < 1e-12
+
+
+def test_per_step_recurrence_is_the_docstring_loop():
+    """s_t = a s_{t-1} + k_t^T v_t, o_t = q_t s_t, y_t = g_t o_t (kernels/kda_kernel.py:8-11), by hand."""
+    from oracle.kda_oracle import per_step_recurrence
+    q = torch.tensor([[[[1.0, 0.0], [0.0, 1.0], [1.0, 1.0]]]])
+    k = torch.tensor([[[[1.0, 0.0], [0.0, 1.0], [1.0, 0.0]]]])
+    v = torch.tensor([[[[2.0, 0.0], [0.0, 3.0], [1.0, 1.0]]]])
+    y, s = per_step_recurrence(q, k, v, None, 0.5, None)
+    # s_0 = [[2,0],[0,0]]; s_1 = [[1,0],[0,3]]; s_2 = [[1.5,1],[0,1.5]]
+    assert torch.allclose(s[0, 0], torch.tensor([[1.5, 1.0], [0.0, 1.5]], dtype=torch.float64))
+    assert torch.allclose(y[0, 0], torch.tensor([[2.0, 0.0], [0.0, 3.0], [1.5, 2.5]], dtype=torch.float64))

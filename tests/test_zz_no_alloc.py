@@ -65,7 +65,7 @@ def test_noalloc_matches_allocating_entry_point_twice(B, H, T, D):
     inp = make_inputs(w, seed=3, device="cuda")
     q, k, v, g, s0 = inp["q"], inp["k"], inp["v"], inp["g"], inp["s0"]
     dec = inp["decay"].expand(B, H, D)
-    y_ref, s_ref = torch.ops.kda_b200.chunk_fwd(q, k, v, g, dec, 0.0, s0, 64, False, True)
+    y_ref, s_ref = torch.ops.kda_b200.chunk_fwd(q, k, v, g, dec, 0.0, s0, 64, 0, True)
     for _ in range(2):
         y, s = _noalloc(q, k, v, g, dec, s0)
         torch.cuda.synchronize()
