@@ -277,7 +277,7 @@ def run_e2e(args, w, rank, world, dev, inp):
 
     from simpletrain_b200 import kda_chunk
 
-    names = ["q", "k", "v", "g", "dy"]
+    names = ["q", "k", "v", "g", "dy"] if w.backward else ["q", "k", "v", "g"]
 
     def pinned_like(t):
         return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device="cpu", pin_memory=True)
@@ -296,14 +296,16 @@ def run_e2e(args, w, rank, world, dev, inp):
         for n in names + ["decay"]:
             dev_in[n].copy_(host[n], non_blocking=True)
         if args.per_step:  # one decay per head, not differentiated
-            leaves = [dev_in[n].requires_grad_(True) for n in ("q", "k", "v", "g")]
+            leaves = [dev_in[n].requires_grad_(w.backward) for n in ("q", "k", "v", "g")]
             y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], dev_in["decay"][:, 0], inp["s0"],
                              per_step=True)
         else:
-            leaves = [dev_in[n].requires_grad_(True) for n in ("q", "k", "v", "g", "decay")]
+            leaves = [dev_in[n].requires_grad_(w.backward) for n in ("q", "k", "v", "g", "decay")]
             y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], inp["s0"])
-        grads = torch.autograd.grad([y], leaves, [dev_in["dy"]])
-        res = [y] + list(grads)
+        if w.backward:
+            res = [y] + list(torch.autograd.grad([y], leaves, [dev_in["dy"]]))
+        else:
+            res = [y]
         if outs is None:
             outs = [pinned_like(r) for r in res]
             d2h = sum(o.numel() * o.element_size() for o in outs)

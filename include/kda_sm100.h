@@ -63,9 +63,10 @@ enum kda_flags {
      (kernels/kda_kernel.py:8-11, :134-180)
          s_t = a s_{t-1} + k_t^T v_t,   o_t = q_t s_t,   y_t = g_t * o_t
      with one decay a per (batch, head): decay == NULL (decay_scalar) or
-     decay_stride_d == 0, and 0.125 <= a <= 1 (checked for decay_scalar; the
-     kernels scale q and k rows by powers of a up to a^-32).  state_out is
-     s_T.  Not with KDA_FLAG_LITERAL; kda_bwd_sm100 takes ddecay == NULL. */
+     decay_stride_d == 0, and 0.125 <= a <= 1 for bf16, 0.9 <= a <= 1 for
+     fp16 (checked for decay_scalar; the kernels scale 16-bit q and k rows by
+     powers a^-32 .. a^32).  state_out is s_T.  Not with KDA_FLAG_LITERAL;
+     kda_bwd_sm100 takes ddecay == NULL. */
   KDA_FLAG_PER_STEP = 1u << 1,
 };
 

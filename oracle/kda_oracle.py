@@ -302,15 +302,16 @@ def per_step_chunk_scan(q, k, v, gate, decay, chunk_size: int = 64,
                         initial_state: Optional[torch.Tensor] = None):
     """Chunked form of the per-step recurrence that the sm_100a kernels run (float64).
 
-    Inside a chunk (local rows i, j < L), with m = REF_ROW,
+    Inside a chunk (local rows i, j < L), with m = REF_ROW, only k is scaled,
 
-        Q^ = diag(a^(i+1-m)) Q,   K~ = diag(a^(m-1-j)) K   (so q^_i . k~_j = a^(i-j) q_i . k_j)
-        O  = tril(Q^ K~^T) V + Q^ (a^m S)
+        K~ = diag(a^(m-1-j)) K                  (so q_i . k~_j = a^(m-1-j) q_i . k_j)
+        O  = diag(a^(i+1-m)) [tril(Q K~^T) V + Q (a^m S)]
         S' = a^L S + a^(L-m) K~^T V
 
-    i.e. the chunk-constant kernels' products on row-scaled q and k tiles,
-    with scalar factors on the carried state.  Every factor lies in
-    [a^(m), a^(-m)], which is why the kernels take 0.125 <= a <= 1.
+    i.e. the chunk-constant kernels' products with a row-scaled k tile, a
+    factor per output row and scalar factors on the carried state.  Every
+    factor lies in [a^m, a^-m], which is why the kernels take 0.125 <= a <= 1
+    (bf16; 0.9 for fp16).
     """
     B, H, T, D = q.shape
     C, m = chunk_size, REF_ROW
@@ -326,11 +327,11 @@ def per_step_chunk_scan(q, k, v, gate, decay, chunk_size: int = 64,
     for t0 in range(0, T, C):
         t1 = min(T, t0 + C)
         L = t1 - t0
-        Qh = Q[:, :, t0:t1] * fq[:, :, :L, None]
+        Qc = Q[:, :, t0:t1]
         Kt = K[:, :, t0:t1] * fk[:, :, :L, None]
         Vc = V[:, :, t0:t1]
-        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
-        O = P @ Vc + Qh @ (a4 ** m * S)
+        P = (Qc @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        O = fq[:, :, :L, None] * (P @ Vc + Qc @ (a4 ** m * S))
         y[:, :, t0:t1] = O * G[:, :, t0:t1] if G is not None else O
         S = a4 ** L * S + a4 ** (L - m) * (Kt.transpose(-1, -2) @ Vc)
     return y, S
@@ -341,14 +342,15 @@ def per_step_manual_backward(q, k, v, gate, decay, chunk_size: int,
                              dstate_T: Optional[torch.Tensor] = None):
     """Explicit backward of ``per_step_chunk_scan`` -- the algorithm of the kernels (float64).
 
-    Gradients of  L = <dy, y> + <dstate_T, s_T>.  With dO = g * dy, the row
-    factors fq, fk and m = REF_ROW:
+    Gradients of  L = <dy, y> + <dstate_T, s_T>.  With the row factors fq, fk,
+    m = REF_ROW and the row-scaled output gradient dO^ = diag(fq) (g * dy)
+    (which the forward-direction pass writes for the reverse pass):
 
-      forward direction:  dg = dy * O
-                          dq = diag(fq) [tril(dO V^T) K~ + dO (a^m S_{c-1})^T]
-      reverse direction:  dk = diag(fk) [tril(dO V^T)^T Q^ + V (a^(L-m) dS_c)^T]
-                          dv = tril(Q^ K~^T)^T dO + K~ (a^(L-m) dS_c)
-                          dS_{c-1} = a^L dS_c + a^m Q^^T dO
+      forward direction:  dg = diag(fq) dy * [tril(Q K~^T) V + Q (a^m S_{c-1})]
+                          dq = tril(dO^ V^T) K~ + dO^ (a^m S_{c-1})^T
+      reverse direction:  dk = diag(fk) [tril(dO^ V^T)^T Q + V (a^(L-m) dS_c)^T]
+                          dv = tril(Q K~^T)^T dO^ + K~ (a^(L-m) dS_c)
+                          dS_{c-1} = a^L dS_c + a^m Q^T dO^
 
     Returns (dq, dk, dv, dg, d_initial_state); the decay is not differentiated.
     """
@@ -369,28 +371,27 @@ def per_step_manual_backward(q, k, v, gate, decay, chunk_size: int,
 
     def tiles(t0, t1):
         L = t1 - t0
-        Qh = Q[:, :, t0:t1] * fq[:, :, :L, None]
         Kt = K[:, :, t0:t1] * fk[:, :, :L, None]
         dO = DY[:, :, t0:t1] * G[:, :, t0:t1] if G is not None else DY[:, :, t0:t1]
-        return L, Qh, Kt, V[:, :, t0:t1], dO
+        return L, Q[:, :, t0:t1], Kt, V[:, :, t0:t1], fq[:, :, :L, None] * dO
 
     for (t0, t1) in chunks:
-        L, Qh, Kt, Vc, dO = tiles(t0, t1)
+        L, Qc, Kt, Vc, dOh = tiles(t0, t1)
         Sh = a4 ** m * S
-        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        P = (Qc @ Kt.transpose(-1, -2)) * causal[:L, :L]
         if G is not None:
-            dg[:, :, t0:t1] = DY[:, :, t0:t1] * (P @ Vc + Qh @ Sh)
-        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
-        dq[:, :, t0:t1] = fq[:, :, :L, None] * (dP @ Kt + dO @ Sh.transpose(-1, -2))
+            dg[:, :, t0:t1] = fq[:, :, :L, None] * DY[:, :, t0:t1] * (P @ Vc + Qc @ Sh)
+        dP = (dOh @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        dq[:, :, t0:t1] = dP @ Kt + dOh @ Sh.transpose(-1, -2)
         S = a4 ** L * S + a4 ** (L - m) * (Kt.transpose(-1, -2) @ Vc)
 
     dS = dstate_T.to(f).clone() if dstate_T is not None else torch.zeros(B, H, D, D, dtype=f)
     for (t0, t1) in reversed(chunks):
-        L, Qh, Kt, Vc, dO = tiles(t0, t1)
+        L, Qc, Kt, Vc, dOh = tiles(t0, t1)
         dSh = a4 ** (L - m) * dS
-        P = (Qh @ Kt.transpose(-1, -2)) * causal[:L, :L]
-        dP = (dO @ Vc.transpose(-1, -2)) * causal[:L, :L]
-        dk[:, :, t0:t1] = fk[:, :, :L, None] * (dP.transpose(-1, -2) @ Qh + Vc @ dSh.transpose(-1, -2))
-        dv[:, :, t0:t1] = P.transpose(-1, -2) @ dO + Kt @ dSh
-        dS = a4 ** L * dS + a4 ** m * (Qh.transpose(-1, -2) @ dO)
+        P = (Qc @ Kt.transpose(-1, -2)) * causal[:L, :L]
+        dP = (dOh @ Vc.transpose(-1, -2)) * causal[:L, :L]
+        dk[:, :, t0:t1] = fk[:, :, :L, None] * (dP.transpose(-1, -2) @ Qc + Vc @ dSh.transpose(-1, -2))
+        dv[:, :, t0:t1] = P.transpose(-1, -2) @ dOh + Kt @ dSh
+        dS = a4 ** L * dS + a4 ** m * (Qc.transpose(-1, -2) @ dOh)
     return dq, dk, dv, dg, dS

@@ -47,11 +47,14 @@ int check_common(int32_t B, int32_t H, int32_t T, int32_t D, int32_t chunk, int3
   return KDA_OK;
 }
 
-// Per-step mode: one decay per (batch, head) within the range the row scaling allows.
-int check_per_step(uint32_t flags, const float *decay, int64_t stride_d, double scalar) {
+// Per-step mode: one decay per (batch, head) within the range the row scaling
+// allows: powers a^-32 .. a^32 of it scale 16-bit operands, so bf16 takes
+// 0.125 <= a <= 1 and fp16 (max 65504, normal above 6.1e-5) 0.9 <= a <= 1.
+int check_per_step(uint32_t flags, int32_t dtype, const float *decay, int64_t stride_d, double scalar) {
   if (!(flags & KDA_FLAG_PER_STEP)) return KDA_OK;
   if (decay != nullptr) return stride_d == 0 ? KDA_OK : KDA_ERR_UNSUPPORTED;
-  return (scalar >= 0.125 && scalar <= 1.0) ? KDA_OK : KDA_ERR_UNSUPPORTED;
+  const double lo = dtype == KDA_DTYPE_F16 ? 0.9 : 0.125;
+  return (scalar >= lo && scalar <= 1.0) ? KDA_OK : KDA_ERR_UNSUPPORTED;
 }
 
 kda::DecaySrc make_decay(const float *ptr, int64_t sb, int64_t sh, int64_t sd, double scalar, int T,
@@ -177,7 +180,7 @@ const char *kda_status_string(int32_t s) {
     case KDA_ERR_BAD_SHAPE: return "invalid shape (negative size, or literal mode with D != chunk)";
     case KDA_ERR_UNSUPPORTED:
       return "unsupported configuration (head dim 64 or 128, chunk 64, dtype bf16/f16; per-step mode: not literal, "
-             "one decay per (batch, head) in [0.125, 1], no decay gradient)";
+             "one decay per (batch, head) in [0.125, 1] (fp16: [0.9, 1]), no decay gradient)";
     case KDA_ERR_BAD_LAYOUT: return "bad layout (innermost stride must be 1, other strides multiples of 8 elements, base 16-byte aligned)";
     case KDA_ERR_WORKSPACE: return "workspace missing or too small";
     case KDA_ERR_CUDA: return "CUDA launch or runtime error";
@@ -208,7 +211,7 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   if (rc) return rc;
   const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   if (literal && p->state_out && (p->T % p->chunk) != 0) return KDA_ERR_BAD_SHAPE;
-  if ((rc = check_per_step(p->flags, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
+  if ((rc = check_per_step(p->flags, p->dtype, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
   if ((p->state_in && !aligned16(p->state_in)) || (p->state_out && !aligned16(p->state_out)))
     return KDA_ERR_BAD_LAYOUT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -254,7 +257,7 @@ int kda_bwd_sm100(const kda_bwd_params *p, kda_stream_t stream) {
   if (rc) return rc;
   const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   if (literal && (p->T % p->chunk) != 0 && p->dstate_out) return KDA_ERR_BAD_SHAPE;
-  if ((rc = check_per_step(p->flags, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
+  if ((rc = check_per_step(p->flags, p->dtype, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
   if ((p->flags & KDA_FLAG_PER_STEP) && p->ddecay) return KDA_ERR_UNSUPPORTED;
   const bool gate = p->g.data != nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -22,10 +22,10 @@
 // Warp 0 loads the two tiles of each chunk into a ring, warp 1 issues one
 // UMMA per chunk (K^T V, literal K V^T, or Q^T dO) into one of two TMEM
 // accumulators, warps 2-9 fold it into the fp32 carry in registers.  In
-// per-step mode (PS) warp 10 first scales the rows of the chunk's K (mode 0)
-// or Q (mode 2) tile like the main kernels (kda_tc_epi.cuh, kRef), and the
-// fold applies the scalar factor: S <- a^64 S + a^(64-kRef) K~^T V, or
-// dS <- a^64 dS + a^kRef Q^^T dO.
+// per-step mode (PS) the fold applies a scalar factor, S <- a^64 S +
+// a^(64-kRef) K~^T V with the k rows scaled first by warp 10 like in the main
+// kernels (kda_tc_epi.cuh, kRef), or dS <- a^64 dS + a^kRef Q^T dO^ with the
+// row-scaled dO^ the forward-direction pass wrote.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -53,8 +53,12 @@ struct AggLayout {
   static constexpr uint32_t TMEM_COLS = 2 * D <= 128 ? 128 : 256;  // two accumulators of D columns
 };
 
+// a row-scaler warp: per-step mode, k tiles (mode 0)
+template <bool PS, int MODE>
+constexpr bool agg_scales() { return PS && MODE == 0; }
+
 template <typename T, int D, bool LIT, bool PS, int MODE, int NS>
-__global__ void __launch_bounds__(kThreads + (PS ? 32 : 0), 1)
+__global__ void __launch_bounds__(kThreads + (agg_scales<PS, MODE>() ? 32 : 0), 1)
     agg_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const AggArgs a,
                   const Queue qu) {
   using L = AggLayout<D, NS>;
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(kThreads + (PS ? 32 : 0), 1)
       for (int k = 0; k < n; ++k) {
         const int s = k % NS, use = k / NS, buf = k & 1;
         const uint32_t st = sb + s * L::STAGE;
-        if (!(mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
+        if (!(mbar_wait(bar((agg_scales<PS, MODE>() ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
               mbar_wait(bar(ACC_FREE + buf), ((k >> 1) & 1) ^ 1, a.status, abort_flag)))
           break;
         tc_fence_after();
@@ -189,15 +193,15 @@ __global__ void __launch_bounds__(kThreads + (PS ? 32 : 0), 1)
       S.store_slot(e, dst);
       if (MODE == 1) Tn.store_slot(e, dst + (Carry<D>::FLOATS / 4) * kEpi);
     }
-  } else if constexpr (PS) {
-    // row scaler: K~ rows a^(kRef-1-j) (mode 0) or Q^ rows a^(i+1-kRef) (mode 2) of tile A
+  } else if constexpr (agg_scales<PS, MODE>()) {
+    // row scaler: K~ rows a^(kRef-1-j) of tile A
     const float l2a = log2f(decay_value(a.decay, b, h, 0));
-    const float e0 = REV ? (float)(lane + 1 - kRef) : (float)(kRef - 1 - lane);
-    const float f0 = pow_log2(l2a, e0), f1 = pow_log2(l2a, REV ? e0 + 32.f : e0 - 32.f);
+    const uint2 f0 = k_row_factor<BF>(l2a, lane), f1 = k_row_factor<BF>(l2a, lane + 32);
     for (int k = 0; k < n; ++k) {
       const int s = k % NS, use = k / NS;
       if (!__all_sync(0xffffffffu, mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
-      scale_tile_rows<L::KB, BF>(sb + s * L::STAGE + L::ST_A, lane, f0, f1);
+      scale_tile_row<L::KB, BF>(sb + s * L::STAGE + L::ST_A, lane, f0);
+      scale_tile_row<L::KB, BF>(sb + s * L::STAGE + L::ST_A, lane + 32, f1);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(SCALED + s));
@@ -221,7 +225,7 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
   auto kern = agg_tc_kernel<T, D, LIT, PS, MODE, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<q.nranges, kThreads + (PS ? 32 : 0), L::SMEM, st>>>(ma, mb, a, q);
+  kern<<<q.nranges, kThreads + (agg_scales<PS, MODE>() ? 32 : 0), L::SMEM, st>>>(ma, mb, a, q);
   count_launches(1);
   return cudaGetLastError();
 }

@@ -18,19 +18,20 @@
 //   dv = K dS + P^T dO         (literal: dS^T K + P^T dO)
 //   dS <- decay^L dS + W
 //
-// Per-step decay (PS, one decay a per stream): q and k rows are scaled in
-// the stage by two extra warps, Q^ = diag(a^(i+1-kRef)) Q, K~ = diag(a^(kRef-1-j)) K,
-// and with them (m = kRef, L the chunk length)
-//   O  = tril(Q^ K~^T) V + Q^ (a^m S)         S <- a^L S + a^(L-m) K~^T V
-//   dq = diag(a^(i+1-m)) [tril(dO V^T) K~ + dO (a^m S)^T]
-//   dk = diag(a^(m-1-j)) [tril(dO V^T)^T Q^ + V (a^(L-m) dS)^T]
-//   dv = tril(Q^ K~^T)^T dO + K~ (a^(L-m) dS)  dS <- a^L dS + a^m Q^^T dO
+// Per-step decay (PS, one decay a per stream): k rows are scaled in the
+// stage by two extra warps, K~ = diag(a^(kRef-1-j)) K, the forward-direction
+// pass writes dO^ = diag(a^(i+1-kRef)) g dy for both passes, and with them
+// (m = kRef, L the chunk length)
+//   O  = diag(a^(i+1-m)) [tril(Q K~^T) V + Q (a^m S)]    -> dg = dy * O
+//   dq = tril(dO^ V^T) K~ + dO^ (a^m S)^T                S <- a^L S + a^(L-m) K~^T V
+//   dk = diag(a^(m-1-j)) [tril(dO^ V^T)^T Q + V (a^(L-m) dS)^T]
+//   dv = tril(Q K~^T)^T dO^ + K~ (a^(L-m) dS)            dS <- a^L dS + a^m Q^T dO^
 // i.e. the same products, scalar factors on the carries and a row factor on
-// dq and dk.  The decay is not differentiated in this mode.
+// O and dk.  The decay is not differentiated in this mode.
 //
 // Warp 0: unit tickets + TMA loads (q, k, v, g, dy) into a two-stage ring;
 // warp 1: tensor memory and the single MMA-issuing thread; warps 2-9:
-// epilogue (PS: warps 10-11 scale q and k).  Outputs leave through TMA
+// epilogue (PS: warps 10-11 scale k).  Outputs leave through TMA
 // stores.  Every wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -66,7 +67,7 @@ struct BwdLayout {
   static constexpr int PANEL = D * 128;  // [D rows x 64 columns] of the carried state operand
   static constexpr int SB = DO + BOX;
   static constexpr int BAR = SB + KB * PANEL;
-  static constexpr int NBAR = 3 * NS + 20;
+  static constexpr int NBAR = 4 * NS + 20;
   static constexpr int RING = BAR + NBAR * 8;
   static constexpr int RED = RING + 16;   // float [D] row sums
   static constexpr int TMEM_SLOT = RED + 4 * D;
@@ -91,7 +92,7 @@ struct RevLayout {
   static constexpr int DK = SB + KB * PANEL;
   static constexpr int DV = DK + BOX;
   static constexpr int BAR = DV + BOX;
-  static constexpr int NBAR = 3 * NS + 20;
+  static constexpr int NBAR = 4 * NS + 20;
   static constexpr int RING = BAR + NBAR * 8;
   static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
@@ -110,11 +111,13 @@ struct RevLayout {
 
 // Producer: tickets and TMA loads of the stage tiles for every chunk of every
 // piece.  Stage slot j (BOX bytes each) is filled from maps[j]; a null map
-// leaves its slot untouched (no gate).
+// leaves its slot untouched (no gate).  KFULL >= 0 (per-step mode): slot 1,
+// the k tile, is loaded first and completes barrier KFULL + stage instead.
 template <int D, int NS, int NT>
 __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, uint32_t sb, int stage_bytes,
                              volatile int *ring, volatile int *abort_flag, const CUtensorMap *const (&maps)[NT],
-                             uint32_t bar_base, int FULL, int EMPTY, int UNIT_FULL0, int UNIT_FREE0) {
+                             uint32_t bar_base, int FULL, int EMPTY, int UNIT_FULL0, int UNIT_FREE0,
+                             int KFULL = -1) {
   constexpr int KB = D / 64, BOX = KB * kTile;
   auto bar = [&](int i) { return bar_base + 8u * i; };
   int ntiles = 0;
@@ -123,7 +126,7 @@ __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, ui
       prefetch_tmap(maps[j]);
       ++ntiles;
     }
-  const uint32_t tx = (uint32_t)(ntiles * BOX);
+  const uint32_t tx = (uint32_t)((ntiles - (KFULL >= 0 ? 1 : 0)) * BOX);
   int gc = 0, i = 0;
   bool ok = true;
   while (ok) {
@@ -144,15 +147,23 @@ __device__ void bwd_producer(const BwdArgs &a, const Queue &qu, bool reverse, ui
         const int s = gc % NS, use = gc / NS;
         if (!(ok = mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag))) break;
         const uint32_t st = sb + s * stage_bytes;
+        if (KFULL >= 0) {
+          mbar_arrive_expect_tx(bar(KFULL + s), (uint32_t)BOX);
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_4d(st + BOX + kb * kTile, maps[1], bar(KFULL + s), 64 * kb, 64 * c, h, b);
+        }
         mbar_arrive_expect_tx(bar(FULL + s), tx);
         for (int j = 0; j < NT; ++j)
-          if (maps[j])
+          if (maps[j] && !(KFULL >= 0 && j == 1))
             for (int kb = 0; kb < KB; ++kb)
               tma_load_4d(st + j * BOX + kb * kTile, maps[j], bar(FULL + s), 64 * kb, 64 * c, h, b);
       }
     }
   }
-  for (int d = gc - 1; d >= 0 && d >= gc - NS; --d) mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+  for (int d = gc - 1; d >= 0 && d >= gc - NS; --d) {
+    mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+    if (KFULL >= 0) mbar_wait(bar(KFULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+  }
 }
 
 // ===========================================================================
@@ -175,7 +186,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
   constexpr uint32_t A_DQ = L::A_QK;
   enum {
     QK_FULL = 2 * NS, DO_FULL, W_FULL, S_READY, KV_FULL, P_FULL, DP_FULL, DPM_FULL, O_FULL, DQ_FULL, OUT_FREE,
-    UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
+    UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED, KFULL = SCALED + NS
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -209,7 +220,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     mbar_init(bar(UNIT_FREE0), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(UNIT_FREE1), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(FIN), 1);
-    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(SCALED + s), 2);
+      mbar_init(bar(KFULL + s), 1);  // per-step: the k tile alone, loaded first
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -225,7 +239,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     if (lane == 0) {
       const CUtensorMap *const maps[5] = {&tq, &tk, &tv, gate ? &tg : nullptr, &tdy};
       bwd_producer<D, NS, 5>(a, qu, false, sb, L::STAGE, ring, abort_flag, maps, sb + L::BAR, FULL, EMPTY, UNIT_FULL0,
-                             UNIT_FREE0);
+                             UNIT_FREE0, PS ? (int)KFULL : -1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -246,7 +260,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
           // the last chunk's O and dq were read: A_QK, A_DP, A_X free
-          if (!(ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
+          if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+                     (!PS || mbar_wait(bar(SCALED + s), use & 1, a.status, abort_flag)) &&
                      mbar_wait(bar(OUT_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
@@ -333,13 +348,15 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
       }
       // per-step: carry factors a^kRef (operand of the first chunk), a^(64-kRef)
-      // (tensor-memory carry -> state), and the dq row factors a^(row+1-kRef)
-      float am = 1.f, au_f = 1.f, rq[2] = {1.f, 1.f};
+      // (tensor-memory carry -> state), the O row factors a^(row+1-kRef) for
+      // rows r0 and r0 + 8, and the factor of this thread's dO row
+      float am = 1.f, au_f = 1.f, rq[2] = {1.f, 1.f}, rdo = 1.f;
       if constexpr (PS) {
         const float l2a = log2f(decay_value(a.decay, b, h, 0));
         am = pow_log2(l2a, (float)kRef);
         au_f = pow_log2(l2a, (float)(64 - kRef));
         for (int ee = 0; ee < 2; ++ee) rq[ee] = pow_log2(l2a, (float)(e.r0 + 8 * ee + 1 - kRef));
+        rdo = pow_log2(l2a, (float)(make_do_row(e.et) + 1 - kRef));
       }
       const bool early = u.early(qu);
       if (early) {
@@ -382,7 +399,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(0, gc);
         // (0) dO (the DO tile's last readers were the previous chunk's MMAs)
-        make_do<D, BF>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate);
+        make_do<D, BF, PS>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate, rdo);
         fence_async_smem();
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
@@ -515,7 +532,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (e.et == 0) KDA_TRACE_EVENT(8, gc);
         tc_fence_after();
         if (gate) {
-          frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, st + L::ST_DY, st + L::ST_DY, true);
+          frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, st + L::ST_DY, st + L::ST_DY, true, rq);
           fence_async_smem();
           named_bar_sync(1, kEpi);
           if (e.et == 0) {
@@ -527,7 +544,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         // (d) dq over the stage's gate tile (read only by the dO step), then a TMA store
         if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
         tc_fence_after();
-        frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false, rq);
+        frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false);
         tc_fence_before();
         mbar_arrive(bar(OUT_FREE));
         fence_async_smem();
@@ -589,9 +606,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       }
     }
   } else if constexpr (PS) {
-    const bool is_q = warp == kThreads / 32;
-    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
-                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
+    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, L::ST_K, warp - kThreads / 32, ring, abort_flag,
+                           a.status, sb + L::BAR, KFULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   if (threadIdx.x == 64) {
     tma_store_wait_all();  // dg / dq stores of the last chunk
@@ -622,7 +638,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
   // tensor memory: A_QK scores, A_DP dP, A_X dk, A_Y dv, A_Z W = Q^T dO
   enum {
     QK_FULL = 2 * NS, QK_FREE, DP_FULL, DP_FREE, W_FULL, W_FREE, DS_READY, DKV_FREE, INTER_FULL, P_FULL, DPM_FULL,
-    DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
+    DKV_FULL, UNIT_FULL0, UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED, KFULL = SCALED + NS
   };
   const int FULL = 0, EMPTY = NS;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -651,7 +667,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     mbar_init(bar(UNIT_FREE0), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(UNIT_FREE1), 1 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(FIN), 1);
-    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(SCALED + s), 2);
+      mbar_init(bar(KFULL + s), 1);  // per-step: the k tile alone, loaded first
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -667,7 +686,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     if (lane == 0) {
       const CUtensorMap *const maps[4] = {&tq, &tk, &tv, &tdo};
       bwd_producer<D, NS, 4>(a, qu, true, sb, L::STAGE, ring, abort_flag, maps, sb + L::BAR, FULL, EMPTY, UNIT_FULL0,
-                             UNIT_FREE0);
+                             UNIT_FREE0, PS ? (int)KFULL : -1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -685,7 +704,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
-          if (!(ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag) &&
+          if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+                     (!PS || mbar_wait(bar(SCALED + s), use & 1, a.status, abort_flag)) &&
                      mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag)))
             break;
           tc_fence_after();
@@ -877,9 +897,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     }
     if (e.et == 0) tma_store_wait_all();
   } else if constexpr (PS) {
-    const bool is_q = warp == kThreads / 32;
-    scaler_role<D, BF, NS>(qu, true, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
-                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
+    scaler_role<D, BF, NS>(qu, true, a.H, a.decay, sb, L::STAGE, L::ST_K, warp - kThreads / 32, ring, abort_flag,
+                           a.status, sb + L::BAR, KFULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   __syncthreads();
   if (warp == 1) {

@@ -21,10 +21,10 @@
 // or from the state published at its range boundary, and publishes its own
 // when it ends mid-stream.
 //
-// Per-step decay (PS): two more warps scale each stage's q and k rows in
-// place after the TMA load (kda_tc_epi.cuh, kRef); the MMAs wait for them,
-// the products are unchanged, and the epilogue applies the carry's scalar
-// factors: operand a^kRef S, S <- a^L S + a^(L-kRef) K~^T V.
+// Per-step decay (PS): two more warps scale each stage's k rows in place
+// after the TMA load, K~ = diag(a^(kRef-1-j)) K (kda_tc_epi.cuh); the MMAs
+// wait for them, the products are unchanged, and the epilogue applies the
+// factors: y = g * a^(i+1-kRef) O, operand a^kRef S, S <- a^L S + a^(L-kRef) K~^T V.
 //
 // Pipelining: O is double-buffered in tensor memory and the epilogue runs
 // "state update of c -> store y_c -> mask P_{c+1}", so the MMAs of chunk c+1
@@ -64,7 +64,7 @@ struct FwdLayout {
   static constexpr int SB = P + kTile;  // S_{c-1}: KB panels of [D rows x 64]
   static constexpr int Y = SB + KB * D * 128;  // NY tiles (BOX each): g in, y out
   static constexpr int BAR = Y + NY * BOX;
-  static constexpr int NBAR = 3 * NS + 2 * NY + 16;
+  static constexpr int NBAR = 4 * NS + 2 * NY + 16;
   static constexpr int RING = BAR + NBAR * 8;  // two (ticket, piece) entries
   static constexpr int TMEM_SLOT = RING + 16;
   static constexpr int ABORT = TMEM_SLOT + 8;
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
   auto bar = [&](int i) { return sb + L::BAR + 8u * i; };
   enum {
     QK_FULL = 2 * NS + 2 * NY, QK_FREE, S_READY, O_FREE0, O_FREE1, KV_FREE, KV_FULL, P_FULL, O_FULL, UNIT_FULL0,
-    UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED
+    UNIT_FULL1, UNIT_FREE0, UNIT_FREE1, FIN, SCALED, KFULL = SCALED + NS
   };
   const int FULL = 0, EMPTY = NS, GFULL = 2 * NS, GEMPTY = 2 * NS + NY;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::ABORT);
@@ -124,7 +124,10 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
     mbar_init(bar(QK_FULL + 11), 2 + kEpi + (PS ? 2 : 0));  // unit ring slots: MMA, gate loader, epilogue, scalers
     mbar_init(bar(QK_FULL + 12), 2 + kEpi + (PS ? 2 : 0));
     mbar_init(bar(QK_FULL + 13), 1);
-    for (int s = 0; s < NS; ++s) mbar_init(bar(SCALED + s), 2);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(SCALED + s), 2);
+      mbar_init(bar(KFULL + s), 1);  // per-step: the k tile alone, loaded first
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&ty);
-      const uint32_t tx = (uint32_t)(3 * L::BOX);
+      const uint32_t tx = (uint32_t)((PS ? 2 : 3) * L::BOX);
       int gc = 0, i = 0;
       bool ok = true;
       while (ok) {
@@ -163,18 +166,25 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
             if (!(ok = mbar_wait(bar(EMPTY + s), (use & 1) ^ 1, a.status, abort_flag))) break;
             KDA_TRACE_EVENT(0, gc);
             const uint32_t st = sb + s * L::STAGE;
+            if (PS) {  // k first, on its own barrier: its row scaling overlaps the q and v loads
+              mbar_arrive_expect_tx(bar(KFULL + s), (uint32_t)L::BOX);
+              for (int kb = 0; kb < KB; ++kb)
+                tma_load_4d(st + L::ST_K + kb * kTile, &tk, bar(KFULL + s), 64 * kb, 64 * c, h, b);
+            }
             mbar_arrive_expect_tx(bar(FULL + s), tx);
             for (int kb = 0; kb < KB; ++kb) {
               tma_load_4d(st + L::ST_Q + kb * kTile, &tq, bar(FULL + s), 64 * kb, 64 * c, h, b);
-              tma_load_4d(st + L::ST_K + kb * kTile, &tk, bar(FULL + s), 64 * kb, 64 * c, h, b);
+              if (!PS) tma_load_4d(st + L::ST_K + kb * kTile, &tk, bar(FULL + s), 64 * kb, 64 * c, h, b);
               tma_load_4d(st + L::ST_V + kb * kTile, &tv, bar(FULL + s), 64 * kb, 64 * c, h, b);
             }
             KDA_TRACE_EVENT(1, gc);
           }
         }
       }
-      for (int d = gc - 1; d >= 0 && d >= gc - NS; --d)
+      for (int d = gc - 1; d >= 0 && d >= gc - NS; --d) {
         mbar_wait(bar(FULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+        if (PS) mbar_wait(bar(KFULL + d % NS), (d / NS) & 1, a.status, abort_flag);
+      }
     } else if (lane == 1) {
       // ------------------------------------------------------- gate loader
       if (gate) prefetch_tmap(&tg);
@@ -219,7 +229,8 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
         for (int c = u.c_begin; c < u.c_end && ok; ++c, ++gc) {
           const int s = gc % NS, use = gc / NS, ph = gc & 1;
           const uint32_t st = sb + s * L::STAGE;
-          ok = mbar_wait(bar((PS ? SCALED : FULL) + s), use & 1, a.status, abort_flag);
+          ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag) &&
+               (!PS || mbar_wait(bar(SCALED + s), use & 1, a.status, abort_flag));
           KDA_TRACE_EVENT(2, gc);
           ok = ok && mbar_wait(bar(QK_FREE), ph ^ 1, a.status, abort_flag);
           if (!ok) break;
@@ -295,13 +306,15 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
         af[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, S.row[r], Ltail, 64);
       }
-      // per-step: operand a^kRef S, U factor a^(L-kRef) (full / tail chunk)
-      float am = 1.f, au_f = 1.f, au_t = 1.f;
+      // per-step: operand a^kRef S, U factor a^(L-kRef) (full / tail chunk),
+      // y row factors a^(row+1-kRef) for rows r0 and r0 + 8
+      float am = 1.f, au_f = 1.f, au_t = 1.f, rq[2] = {1.f, 1.f};
       if constexpr (PS) {
         const float l2a = log2f(decay_value(a.decay, b, h, 0));
         am = pow_log2(l2a, (float)kRef);
         au_f = pow_log2(l2a, (float)(64 - kRef));
         au_t = pow_log2(l2a, (float)(Ltail - kRef));
+        for (int ee = 0; ee < 2; ++ee) rq[ee] = pow_log2(l2a, (float)(e.r0 + 8 * ee + 1 - kRef));
       }
       const bool early = u.early(qu);
       if (early) {
@@ -416,6 +429,10 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
           for (int jj = 0; jj < W / 8; ++jj)
             for (int ee = 0; ee < 2; ++ee) {
               float o0 = fo.v(ee, jj, 0), o1 = fo.v(ee, jj, 1);
+              if constexpr (PS) {
+                o0 *= rq[ee];
+                o1 *= rq[ee];
+              }
               if (gate) {
                 const float2 g2 = unpack2(gv[2 * jj + ee], BF);
                 o0 *= g2.x;
@@ -452,9 +469,8 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
     }
   } else if constexpr (PS) {
     // ------------------------------------------------------- row scalers
-    const bool is_q = warp == kFwdThreads / 32;
-    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, is_q ? L::ST_Q : L::ST_K, is_q, ring, abort_flag,
-                           a.status, sb + L::BAR, FULL, SCALED, UNIT_FULL0, UNIT_FREE0);
+    scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, L::ST_K, warp - kFwdThreads / 32, ring,
+                           abort_flag, a.status, sb + L::BAR, KFULL, SCALED, UNIT_FULL0, UNIT_FREE0);
   }
   __syncthreads();
   if (warp == 1) {
@@ -504,11 +520,16 @@ int fwd_ctas_per_sm() {
 
 }  // namespace
 
+// Stage and gate-tile counts of the per-step kernels.
+constexpr int kPsNS = 2, kPsNY = 4;
+
 int fwd_tc_occupancy(int D, int dtype, bool literal, bool per_step) {
   const bool bf = dtype == KDA_DTYPE_BF16;
   if (per_step) {
-    if (D == 64) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, true>() : fwd_ctas_per_sm<__half, 64, false, true>();
-    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, true>() : fwd_ctas_per_sm<__half, 128, false, true>();
+    if (D == 64)
+      return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, false, true>() : fwd_ctas_per_sm<__half, 64, false, true>();
+    return bf ? fwd_ctas_per_sm<__nv_bfloat16, 128, false, true, kPsNS, kPsNY>()
+              : fwd_ctas_per_sm<__half, 128, false, true, kPsNS, kPsNY>();
   }
   if (D == 64) {
     if (literal) return bf ? fwd_ctas_per_sm<__nv_bfloat16, 64, true, false>() : fwd_ctas_per_sm<__half, 64, true, false>();
@@ -523,8 +544,8 @@ cudaError_t launch_fwd_tc(const FwdArgs &a, const tc::Queue &q, int grid, int dt
     if (a.D == 64)
       return bf ? fwd_tc_launch<__nv_bfloat16, 64, false, true>(a, q, grid, st)
                 : fwd_tc_launch<__half, 64, false, true>(a, q, grid, st);
-    return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, true>(a, q, grid, st)
-              : fwd_tc_launch<__half, 128, false, true>(a, q, grid, st);
+    return bf ? fwd_tc_launch<__nv_bfloat16, 128, false, true, kPsNS, kPsNY>(a, q, grid, st)
+              : fwd_tc_launch<__half, 128, false, true, kPsNS, kPsNY>(a, q, grid, st);
   }
   if (a.D == 64) {
     if (a.literal)

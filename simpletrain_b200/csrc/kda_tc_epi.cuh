@@ -229,12 +229,17 @@ struct Carry {
 static_assert(kQ == 2 || kQ == 4, "column groups of 64 or 32 (D=128) and 32 or 16 (D=64)");
 
 // ---------------------------------------------------------- tile helpers --
+// Row of the DO tile that epilogue thread `et` writes in make_do.
+__device__ __forceinline__ int make_do_row(int et) { return et / (kEpi / 64); }
+
 // dO = dy * g (or dy) into the DO tile; all epilogue threads, eight per row.
-template <int D, bool BF>
-__device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_t do_tile, bool gate) {
+// ROWF: also times rowf, this thread's row factor (per-step mode).
+template <int D, bool BF, bool ROWF = false>
+__device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_t do_tile, bool gate,
+                        float rowf = 1.f) {
   constexpr int TPR = kEpi / 64;            // threads per row
   constexpr int N = 8 * (D / 64) / TPR;    // 16-byte chunks per thread
-  const int row = e.et / TPR, q = e.et % TPR;
+  const int row = make_do_row(e.et), q = e.et % TPR;
   uint32_t off[N];
   uint4 y[N], g[N];
   for (int i = 0; i < N; ++i) {  // all loads first: the shared-memory accesses are ordered asm
@@ -249,7 +254,13 @@ __device__ void make_do(const Epi &e, uint32_t g_tile, uint32_t dy_tile, uint32_
       const uint32_t *pg = &g[i].x;
       for (int k = 0; k < 4; ++k) {
         const float2 a = unpack2(py[k], BF), b = unpack2(pg[k], BF);
-        py[k] = pack2(a.x * b.x, a.y * b.y, BF);
+        py[k] = ROWF ? pack2(rowf * (a.x * b.x), rowf * (a.y * b.y), BF) : pack2(a.x * b.x, a.y * b.y, BF);
+      }
+    } else if (ROWF) {
+      uint32_t *py = &y[i].x;
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = unpack2(py[k], BF);
+        py[k] = pack2(rowf * a.x, rowf * a.y, BF);
       }
     }
     st_shared_v4(do_tile + off[i], y[i].x, y[i].y, y[i].z, y[i].w);
@@ -305,36 +316,61 @@ __device__ __forceinline__ void frag_to_tile(const Epi &e, uint32_t taddr, uint3
 
 // ------------------------------------------------------ per-step decay --
 // Per-step semantics (one decay a per stream, s_t = a s_{t-1} + k_t^T v_t)
-// run on the chunk kernels with row-scaled q and k tiles
-//   Q^ = diag(a^(i+1-kRef)) Q,   K~ = diag(a^(kRef-1-j)) K,
-// so that q^_i . k~_j = a^(i-j) q_i . k_j and every factor stays within
-// [a^kRef, a^-kRef]; the carried state picks up scalar factors only.
+// run on the chunk kernels with a row-scaled k tile,
+//   K~ = diag(a^(kRef-1-j)) K,   so that q_i . k~_j = a^(i-j) * a^(kRef-1-i) q_i . k_j,
+// a factor a^(i+1-kRef) on each output row (or on the rows of dO, which the
+// backward then carries as dO^ = diag(a^(i+1-kRef)) g dy), and scalar factors
+// on the carried state.  Every factor stays within [a^kRef, a^-kRef].
 constexpr int kRef = 32;
 
 // a^e for the per-step decay of a stream (log2 a given)
 __device__ __forceinline__ float pow_log2(float l2a, float e) { return exp2f(l2a * e); }
 
-// Scales rows `lane` and `lane + 32` of a [64 x 64 KB] 16-bit tile (KB
-// swizzled boxes) in place by f0 and f1.  A row is one 128-byte line of each
-// box whatever the swizzle, so a row factor needs no column mapping; each lane
-// starts at a different 16-byte chunk so that a warp's accesses cover all banks.
+// A factor f as a pair of 16-bit pairs (f_hi, f_lo): f_hi = f rounded,
+// f_lo = the remainder f - f_hi rounded, each in both halves.
+template <bool BF>
+__device__ __forceinline__ uint2 split_factor(float f) {
+  const uint32_t hi = pack2(f, f, BF);
+  const float r = f - unpack2(hi, BF).x;
+  return make_uint2(hi, pack2(r, r, BF));
+}
+
+// x * f for a pair of 16-bit values: fma(x, f_hi, x f_lo) rounds once, and
+// x f_lo carries the factor's rounding error to within ~2^-16 of x f, so the
+// result is x * f rounded to nearest (two packed instructions per pair).
+template <bool BF>
+__device__ __forceinline__ uint32_t mul2_split(uint32_t x, uint2 f) {
+  uint32_t d;
+  if constexpr (BF)
+    asm("{\n\t.reg .b32 t;\n\tmul.rn.bf16x2 t, %1, %3;\n\tfma.rn.bf16x2 %0, %1, %2, t;\n\t}"
+        : "=r"(d) : "r"(x), "r"(f.x), "r"(f.y));
+  else
+    asm("{\n\t.reg .b32 t;\n\tmul.rn.f16x2 t, %1, %3;\n\tfma.rn.f16x2 %0, %1, %2, t;\n\t}"
+        : "=r"(d) : "r"(x), "r"(f.x), "r"(f.y));
+  return d;
+}
+
+// Scales row `row` of a [64 x 64 KB] 16-bit tile (KB swizzled boxes) in place
+// by f (split_factor form).  A row is one 128-byte line of each box whatever
+// the swizzle, so a row factor needs no column mapping; lanes holding rows
+// that share banks start at different 16-byte chunks so that a warp's
+// accesses cover all banks.
 template <int KB, bool BF>
-__device__ __forceinline__ void scale_tile_rows(uint32_t tile, int lane, float f0, float f1) {
-  for (int kb = 0; kb < KB; ++kb)
-    for (int hh = 0; hh < 2; ++hh) {
-      const uint32_t line = tile + (uint32_t)(kb * kTile) + (uint32_t)((lane + 32 * hh) * 128);
-      const float f = hh ? f1 : f0;
-      uint4 v[8];
-      for (int c = 0; c < 8; ++c) v[c] = ld_shared_v4(line + (((c + lane) & 7) << 4));
-      for (int c = 0; c < 8; ++c) {
-        uint32_t *pv = &v[c].x;
-        for (int k = 0; k < 4; ++k) {
-          const float2 x = unpack2(pv[k], BF);
-          pv[k] = pack2(f * x.x, f * x.y, BF);
-        }
-        st_shared_v4(line + (((c + lane) & 7) << 4), v[c].x, v[c].y, v[c].z, v[c].w);
-      }
-    }
+__device__ __forceinline__ void scale_tile_row(uint32_t tile, int row, uint2 f) {
+  for (int kb = 0; kb < KB; ++kb) {
+    const uint32_t line = tile + (uint32_t)(kb * kTile) + (uint32_t)(row * 128);
+    uint4 v[8];
+    for (int c = 0; c < 8; ++c) v[c] = ld_shared_v4(line + (((c + row) & 7) << 4));
+    for (int c = 0; c < 8; ++c)
+      st_shared_v4(line + (((c + row) & 7) << 4), mul2_split<BF>(v[c].x, f), mul2_split<BF>(v[c].y, f),
+                   mul2_split<BF>(v[c].z, f), mul2_split<BF>(v[c].w, f));
+  }
+}
+
+// Per-step factor a^(kRef-1-row) of row `row` of the k tile (log2 a given)
+template <bool BF>
+__device__ __forceinline__ uint2 k_row_factor(float l2a, int row) {
+  return split_factor<BF>(pow_log2(l2a, (float)(kRef - 1 - row)));
 }
 
 // ------------------------------------------------------------ scheduling --
@@ -461,13 +497,14 @@ __device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, c
   }
 }
 
-// Per-step mode: one warp scales the q (is_q) or the k tile of every stage
-// after its TMA load and before its MMAs (which wait on `SCALED + stage`,
-// one arrival per scaler warp).  Units come from the same two-entry ring as
-// the other roles; each warp frees a ring entry with one arrival.
+// Per-step mode: two warps scale the k tile of every stage (warp `half`
+// rows 32 half .. 32 half + 31) after its TMA load and before its MMAs (which
+// wait on `SCALED + stage`, one arrival per scaler warp).  Units come from
+// the same two-entry ring as the other roles; each warp frees a ring entry
+// with one arrival.
 template <int D, bool BF, int NS>
 __device__ void scaler_role(const Queue &qu, bool reverse, int H, const DecaySrc &dec, uint32_t sb,
-                            int stage_bytes, uint32_t tile_off, bool is_q, volatile int *ring,
+                            int stage_bytes, uint32_t tile_off, int half, volatile int *ring,
                             volatile int *abort_flag, int32_t *status, uint32_t bar_base, int FULL, int SCALED,
                             int UNIT_FULL0, int UNIT_FREE0) {
   const int lane = threadIdx.x & 31;
@@ -482,14 +519,13 @@ __device__ void scaler_role(const Queue &qu, bool reverse, int H, const DecaySrc
     if (t >= qu.nranges) break;
     const Piece u = piece_of(qu, span_of(qu, t, reverse), p, reverse);
     const int b = u.stream / H, h = u.stream - b * H;
-    const float l2a = log2f(decay_value(dec, b, h, 0));
-    const float e0 = is_q ? (float)(lane + 1 - kRef) : (float)(kRef - 1 - lane);
-    const float f0 = pow_log2(l2a, e0), f1 = pow_log2(l2a, is_q ? e0 + 32.f : e0 - 32.f);
+    const int row = lane + 32 * half;
+    const uint2 f = k_row_factor<BF>(log2f(decay_value(dec, b, h, 0)), row);
     bool ok = true;
     for (int k = 0; k < u.c_end - u.c_begin; ++k, ++gc) {
       const int s = gc % NS, use = gc / NS;
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(FULL + s), use & 1, status, abort_flag)))) break;
-      scale_tile_rows<D / 64, BF>(sb + (uint32_t)(s * stage_bytes) + tile_off, lane, f0, f1);
+      scale_tile_row<D / 64, BF>(sb + (uint32_t)(s * stage_bytes) + tile_off, row, f);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(SCALED + s));

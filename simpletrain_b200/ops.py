@@ -179,16 +179,20 @@ def decay_as_bhd(decay: Union[float, Tensor], B: int, H: int, D: int) -> Tuple[O
     return torch.broadcast_to(d, (B, H, D)), 0.0
 
 
-def per_step_decay(decay: Union[float, Tensor], B: int, H: int, D: int) -> Tuple[Optional[Tensor], float]:
+def per_step_decay(decay: Union[float, Tensor], B: int, H: int, D: int,
+                   dtype: torch.dtype = torch.bfloat16) -> Tuple[Optional[Tensor], float]:
     """Per-step decay as (fp32 [B,H,D] view constant along D, or None, scalar).
 
-    Accepted: a float in [0.125, 1], or a tensor of shape (), (H,) (per head)
-    or anything broadcastable to (B, H, 1) (one decay per batch and head).
+    Accepted: a float in [0.125, 1] (fp16 inputs: [0.9, 1], the powers
+    a^-32 .. a^32 the kernels scale q and k rows by must fit fp16), or a tensor
+    of shape (), (H,) (per head) or anything broadcastable to (B, H, 1) (one
+    decay per batch and head) with values in the same range.
     """
     if not torch.is_tensor(decay):
         a = float(decay)
-        if not 0.125 <= a <= 1.0:
-            raise ValueError(f"per-step decay must lie in [0.125, 1], got {a}")
+        lo = 0.9 if dtype == torch.float16 else 0.125
+        if not lo <= a <= 1.0:
+            raise ValueError(f"per-step decay must lie in [{lo}, 1] for {dtype}, got {a}")
         return None, a
     if decay.requires_grad:
         raise NotImplementedError("per-step mode does not differentiate the decay")
@@ -231,7 +235,7 @@ def kda_chunk(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
             f"at non-singleton dimension 3")
     if reference_exact and output_final_state and T % chunk_size:
         raise ValueError("reference_exact: the final state of a ragged last chunk is not defined")
-    dt, ds = per_step_decay(decay, B, H, D) if per_step else decay_as_bhd(decay, B, H, D)
+    dt, ds = per_step_decay(decay, B, H, D, q.dtype) if per_step else decay_as_bhd(decay, B, H, D)
     if initial_state is not None and initial_state.shape != (B, H, D, D):
         raise ValueError(f"initial_state must be [B, H, D, D] = {(B, H, D, D)}")
     mode = MODE_PER_STEP if per_step else (MODE_LITERAL if reference_exact else MODE_CORRECTED)

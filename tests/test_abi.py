@@ -110,6 +110,7 @@ def _bwd_params(**kw):
     dict(flags=_ffi.KDA_FLAG_PER_STEP | _ffi.KDA_FLAG_LITERAL),            # two semantics at once
     dict(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=0.1),                   # below the row-scaling range
     dict(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=1.5),
+    dict(flags=_ffi.KDA_FLAG_PER_STEP, decay_scalar=0.8, dtype=_ffi.KDA_DTYPE_F16),   # fp16 range
     dict(flags=_ffi.KDA_FLAG_PER_STEP, decay=0x10000, decay_stride_d=1),    # varies along the key channels
 ])
 def test_per_step_argument_checks(kw):

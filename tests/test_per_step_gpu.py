@@ -142,6 +142,15 @@ def test_per_step_forward_backward_small(B, H, T, D, gate, dkind, with_s0):
     compare(run_gpu(q, k, v, g, decay, s0, dy, dsT), oracle_recurrence(q, k, v, g, decay, s0, dy, dsT))
 
 
+def test_per_step_fp16_inputs():
+    q, k, v, g, dy, _ = _rand(1, 2, 160, 128, seed=16, dtype=torch.float16)
+    s0 = torch.randn(1, 2, 128, 128) * 0.05
+    dsT = torch.randn(1, 2, 128, 128) * 0.1
+    got = run_gpu(q, k, v, g, 0.93, s0, dy, dsT)
+    assert got["y"].dtype == torch.float16
+    compare(got, oracle_recurrence(q, k, v, g, 0.93, s0, dy, dsT))
+
+
 LONG = [
     (1, 1, 4096, 128, True, "0.999", True),
     (1, 2, 3000, 64, True, "head", False),
@@ -192,13 +201,14 @@ def test_per_step_dropin_semantics(monkeypatch):
     assert max_rel(y.double().cpu(), ref["y"]) <= TOL_LOWP
 
 
-@pytest.mark.parametrize("decay,exc", [
-    (0.05, ValueError),                                   # below the supported range
-    (1.5, ValueError),
-    (torch.full((2, 64), 0.9), ValueError),               # per key channel: not one per head
+@pytest.mark.parametrize("decay,exc,dtype", [
+    (0.05, ValueError, torch.bfloat16),                   # below the supported range
+    (1.5, ValueError, torch.bfloat16),
+    (0.8, ValueError, torch.float16),                     # fp16 takes [0.9, 1]
+    (torch.full((2, 64), 0.9), ValueError, torch.bfloat16),  # per key channel: not one per head
 ])
-def test_per_step_rejects_unsupported_decay(decay, exc):
-    q = torch.randn(1, 2, 64, 64, device=DEV, dtype=torch.bfloat16)
+def test_per_step_rejects_unsupported_decay(decay, exc, dtype):
+    q = torch.randn(1, 2, 64, 64, device=DEV, dtype=dtype)
     d = decay.to(DEV) if torch.is_tensor(decay) else decay
     with pytest.raises(exc):
         kda_chunk(q, q, q, None, d, None, per_step=True)
