@@ -264,6 +264,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                      (!PS || mbar_wait(bar(SCALED + s), use & 1, a.status, abort_flag)) &&
                      mbar_wait(bar(OUT_FREE), ph ^ 1, a.status, abort_flag)))
             break;
+          KDA_TRACE_EVENT(13, gc);
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
@@ -272,18 +273,21 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           mma_commit(bar(QK_FULL));
           // W = Q^T dO and dP = dO V^T once dO is staged
           if (!(ok = mbar_wait(bar(DO_FULL), ph, a.status, abort_flag))) break;
+          KDA_TRACE_EVENT(14, gc);
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
             mma_f16(tmem + L::A_DP, sdesc_k(sb + L::DO + off), sdesc_k(st + L::ST_V + off), id_dp, ks > 0);
           }
           mma_commit(bar(DP_FULL));
-          for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + L::A_Y, sdesc_mn(st + L::ST_Q + ks * 2048, kTile), sdesc_mn(sb + L::DO + ks * 2048, kTile),
-                    id_w, ks > 0);
+          if (want_dd)  // W feeds only the decay gradient
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f16(tmem + L::A_Y, sdesc_mn(st + L::ST_Q + ks * 2048, kTile),
+                      sdesc_mn(sb + L::DO + ks * 2048, kTile), id_w, ks > 0);
           mma_commit(bar(W_FULL));
           // intra-chunk parts while the epilogue steps the state: O = P V, dq = dP K
           if (!(ok = mbar_wait(bar(P_FULL), ph, a.status, abort_flag))) break;
+          KDA_TRACE_EVENT(15, gc);
           tc_fence_after();
           for (int ks = 0; ks < 4; ++ks)
             mma_f16(tmem + L::A_X, sdesc_k(sb + L::P + ks * 32), sdesc_mn(st + L::ST_V + ks * 2048, kTile), id_pv,
@@ -295,6 +299,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                     ks > 0);
           // inter-chunk parts: O += Q S_{c-1}, dq += dO S_{c-1}^T, S += K^T V
           if (!(ok = mbar_wait(bar(S_READY), ph, a.status, abort_flag))) break;
+          KDA_TRACE_EVENT(17, gc);
           tc_fence_after();
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
@@ -399,10 +404,14 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(0, gc);
         // (0) dO (the DO tile's last readers were the previous chunk's MMAs)
+        if (e.et == 0) KDA_TRACE_EVENT(27, gc);
         make_do<D, BF, PS>(e, st + L::ST_G, st + L::ST_DY, sb + L::DO, gate, rdo);
+        if (e.et == 0) KDA_TRACE_EVENT(28, gc);
         fence_async_smem();
+        if (e.et == 0) KDA_TRACE_EVENT(29, gc);
         named_bar_sync(1, kEpi);
         if (e.et == 0) {
+          KDA_TRACE_EVENT(30, gc);
           mbar_arrive(bar(DO_FULL));
           // dO also goes to the workspace, where the reverse pass reads it
           for (int kb = 0; kb < L::KB; ++kb) tma_store_4d(&tdo, sb + L::DO + kb * kTile, 64 * kb, t0, h, b);
@@ -414,6 +423,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (e.et == 0) KDA_TRACE_EVENT(5, gc);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
+        if (e.et == 0) KDA_TRACE_EVENT(31, gc);
         if (!(ok = mbar_wait(bar(DP_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(6, gc);
         tc_fence_after();
@@ -488,7 +498,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                              pack2(sop * __uint_as_float(u32[8 * j + 6]), sop * __uint_as_float(u32[8 * j + 7]), BF));
               for (int k = 0; k < 16; ++k) {
                 const float sv = __uint_as_float(u32[k]);
-                if constexpr (!PS) Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
+                if (!PS && want_dd) Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
                 u32[k] = __float_as_uint(stm * sv);
               }
               tmem_st_32x32b_x16_nowait(tmem + e.lane_off + L::A_Z + col0, u32);
@@ -513,7 +523,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
             Sp.template write_operand<BF>(e, sb + L::SB, sop);
             for (int r = 0; r < Carry<D>::NR; ++r)
               for (int k = 0; k < Carry<D>::NV; ++k) {
-                if constexpr (!PS) Td.x[r][k] = alr[r] * fmaf(Lf, Sp.x[r][k], Td.x[r][k]);
+                if (!PS && want_dd) Td.x[r][k] = alr[r] * fmaf(Lf, Sp.x[r][k], Td.x[r][k]);
                 Sp.x[r][k] *= PS ? stm : alr[r];
               }
             Sp.tmem_store(e, tmem, L::A_Z);
