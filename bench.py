@@ -445,6 +445,42 @@ def run_reference(args, w, rank, world):
     }
 
 
+def run_layer(args):
+    """The KDA layer forward + backward at the 1b shape (d_model 2560, 10 heads of
+    128, B=16, T=2048, bf16), structured as SimpleTrain's layer (four projection
+    GEMMs, the mean decay read back with .item()) and fused (one projection GEMM,
+    decay on the device, free transpose): one JSON line each, CUDA-event time."""
+    from simpletrain_b200.kda_layer import KDALayer, fused_forward, unfused_forward
+
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    B, T, Dm, H, Dh = 16, 2048, 2560, 10, 128
+    layer = KDALayer(Dm, H, Dh).to(dev).to(torch.bfloat16)
+    with torch.no_grad():
+        layer.g_proj.weight.normal_(0.0, Dm ** -0.5)
+    x = torch.randn(B, T, Dm, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(B, T, Dm, device=dev, dtype=torch.bfloat16)
+    for name, fwd, syncs in (("layer-structure (4 GEMMs, .item())", unfused_forward, 1),
+                             ("fused (1 GEMM, no host sync)", fused_forward, 0)):
+        def step():
+            y = fwd(layer, x)
+            y.backward(dy)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        n = args.steps or 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        print(json.dumps({"layer": name, "ms_per_step": round(ms, 4), "tokens_per_s": round(B * T / (ms / 1e3), 1),
+                          "host_syncs_per_step": syncs, "pass": "fwd+bwd",
+                          "shape": {"B": B, "T": T, "d_model": Dm, "H": H, "D_head": Dh}}), flush=True)
+
+
 def run_fused_ops(args):
     """One JSON line per fused op (fwd and bwd): HBM GB/s against the measured peak.
 
@@ -518,10 +554,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--fused-ops", action="store_true",
                     help="measure the fused silu*mul / RMSNorm / cross-entropy ops instead (one line each)")
+    ap.add_argument("--layer", action="store_true",
+                    help="measure the KDA layer fwd+bwd, structured as SimpleTrain's and fused (one line each)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.fused_ops:
         run_fused_ops(args)
+        return
+    if args.layer:
+        run_layer(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

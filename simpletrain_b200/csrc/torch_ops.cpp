@@ -41,6 +41,17 @@ bool abi_layout_ok(const Tensor &t) {
 
 Tensor prep(const Tensor &t) { return abi_layout_ok(t) ? t : t.contiguous(); }
 
+// New [B, H, T, D] tensor in the dimension order of `like`: its strides when
+// they are dense, else [B, T, H, D] memory when `like` is time-major (the KDA
+// layer's projection views, models/kimi_k3.py:99-102, dense or not), else
+// contiguous.  Keeps the layer's transpose + contiguous() after the scan free.
+Tensor empty_in_order_of(const Tensor &like) {
+  if (like.is_non_overlapping_and_dense()) return at::empty_like(like);
+  if (like.stride(1) < like.stride(2))
+    return at::empty({like.size(0), like.size(2), like.size(1), like.size(3)}, like.options()).transpose(1, 2);
+  return at::empty(like.sizes(), like.options());
+}
+
 optional<Tensor> prep(const optional<Tensor> &t) {
   if (!t.has_value()) return t;
   return prep(*t);
@@ -125,7 +136,7 @@ std::tuple<Tensor, Tensor> chunk_fwd(const Tensor &q_, const Tensor &k_, const T
   const Tensor q = prep(q_), k = prep(k_), v = prep(v_);
   const optional<Tensor> g = prep(g_);
   const int64_t B = q.size(0), H = q.size(1), T = q.size(2), D = q.size(3);
-  const Tensor y = prep(at::empty_like(q));  // like the reference: keeps q's memory order
+  const Tensor y = prep(empty_in_order_of(q));  // like the reference: keeps q's memory order
   const auto f32 = q.options().dtype(at::kFloat);
   const Tensor s_out = want_state ? at::empty({B, H, D, D}, f32) : at::empty({0}, f32);
   const optional<Tensor> s_in = s0.has_value() ? optional<Tensor>(s0->contiguous().to(at::kFloat)) : c10::nullopt;
@@ -158,8 +169,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> chunk_bwd(
   const Tensor q = prep(q_), k = prep(k_), v = prep(v_), dy = prep(dy_);
   const optional<Tensor> g = prep(g_);
   const int64_t B = q.size(0), H = q.size(1), T = q.size(2), D = q.size(3);
-  const Tensor dq = prep(at::empty_like(q)), dk = prep(at::empty_like(k)), dv = prep(at::empty_like(v));
-  const Tensor dg = g.has_value() ? prep(at::empty_like(*g)) : at::empty({0}, q.options());
+  const Tensor dq = prep(empty_in_order_of(q)), dk = prep(empty_in_order_of(k)), dv = prep(empty_in_order_of(v));
+  const Tensor dg = g.has_value() ? prep(empty_in_order_of(*g)) : at::empty({0}, q.options());
   const bool need_ddecay = need_ddecay_ && decay.has_value();
   const auto f32 = q.options().dtype(at::kFloat);
   const Tensor ddecay = need_ddecay ? at::empty({B, H, D}, f32) : at::empty({0}, f32);

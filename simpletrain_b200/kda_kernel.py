@@ -85,7 +85,7 @@ def _decay_arg(decay: Union[float, torch.Tensor], B: int, H: int, D: int):
         return float(decay)
     d = decay.float()
     if d.dim() == 0:
-        return d.expand(B, H, D)
+        return d.reshape(1, 1, 1).expand(B, H, D)
     if d.shape[-1] != 1 and D != 1:
         raise NotImplementedError(
             "decay tensors must broadcast as [B, H, D, 1] (one factor per key-channel row)")
