@@ -45,8 +45,8 @@ int st_rmsnorm_residual_bwd(const void *x, const void *weight, const float *rstd
 size_t st_rmsnorm_residual_bwd_scratch(int64_t N, int64_t D);
 
 /* Rows of logits [N, V]: lse[n] = log sum_v exp(logits[n, v]) and
-   loss[n] = lse[n] - logits[n, labels[n]] (fp32), by a max sweep and a
-   sum-of-exponentials sweep over the row (kernels/fused_ops.py:209-238);
+   loss[n] = lse[n] - logits[n, labels[n]] (fp32), by one pass over the row
+   with a running maximum and sum of exponentials (kernels/fused_ops.py:209-238);
    when probs is not NULL it also receives softmax(logits) in the logits
    dtype (kernels/fused_ops.py:249-263).  labels are int64; a label outside
    [0, V) gives a NaN loss for its row. */

@@ -8,9 +8,9 @@
 //   RMSNorm + res   one warp per row, two sweeps of the row (the second hits
 //                   L2); the weight gradient is summed per CTA in registers,
 //                   then across CTAs in a fixed order  (kernels/fused_ops.py:129-145)
-//   cross-entropy   one CTA per row: a max sweep over the vocabulary from HBM,
-//                   a sum-of-exp sweep that hits L2, an optional softmax
-//                   sweep; the backward recomputes softmax from the saved
+//   cross-entropy   one CTA per row: one pass over the vocabulary from HBM
+//                   with a running maximum and sum of exponentials, an optional
+//                   softmax sweep; the backward recomputes softmax from the saved
 //                   log-sum-exp                        (kernels/fused_ops.py:209-263)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -291,49 +291,71 @@ int rmsnorm_bwd_grid(int64_t N) {
 }
 
 // ---------------------------------------------------------- cross-entropy
-__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sm) {
-  for (int o = 16; o > 0; o >>= 1) {
-    const float u = __shfl_xor_sync(0xffffffffu, v, o);
-    v = is_max ? fmaxf(v, u) : v + u;
-  }
-  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = sm[0];
-  for (int i = 1; i < kBlock / 32; ++i) r = is_max ? fmaxf(r, sm[i]) : r + sm[i];
-  __syncthreads();  // sm is reused by the next reduction
-  return r;
+// 2^x by the hardware approximation (relative error ~2^-22); e^x = 2^(x log2 e)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Running (max m, sum s of exp(x - m)) pairs, merged: one exponential per
+// element and one rescale when the maximum grows.  m = -inf means "no
+// elements yet" (s = 0).
+__device__ __forceinline__ void lse_merge(float &m, float &s, float m2, float s2) {
+  const float M = fmaxf(m, m2);
+  if (M == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * ex2_approx((m - M) * kLog2e)) +
+      (m2 == -INFINITY ? 0.f : s2 * ex2_approx((m2 - M) * kLog2e));
+  m = M;
 }
 
+__device__ __forceinline__ void block_lse(float &m, float &s, float *sm_m, float *sm_s) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, m2, s2);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm_m[threadIdx.x >> 5] = m;
+    sm_s[threadIdx.x >> 5] = s;
+  }
+  __syncthreads();
+  m = sm_m[0];
+  s = sm_s[0];
+  for (int i = 1; i < kBlock / 32; ++i) lse_merge(m, s, sm_m[i], sm_s[i]);
+}
+
+// One CTA per row.  One pass over the row (HBM) keeps each thread's running
+// maximum and sum of exponentials, rescaled once per 16-byte vector whose
+// maximum exceeds the running one; the pairs are merged across the block.
 template <bool BF, bool VEC>
 __global__ void __launch_bounds__(kBlock)
     ce_fwd_kernel(const void *logits, const int64_t *labels, float *loss, float *lse_out, void *probs, int64_t V) {
-  __shared__ float sm[kBlock / 32];
+  __shared__ float sm_m[kBlock / 32], sm_s[kBlock / 32];
   const int64_t row = blockIdx.x, base = row * V;
   const uint4 *l4 = reinterpret_cast<const uint4 *>(logits) + base / 8;
-  // sweep 1 (HBM): the row maximum
-  float m = -INFINITY;
+  float m = -INFINITY, s = 0.f;
   if (VEC) {
     for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
       float f[8];
       unpack8<BF>(__ldg(l4 + i), f);
-      for (int k = 0; k < 8; ++k) m = fmaxf(m, f[k]);
+      float mv = f[0];
+      for (int k = 1; k < 8; ++k) mv = fmaxf(mv, f[k]);
+      if (mv > m) {
+        s = (m == -INFINITY) ? 0.f : s * ex2_approx((m - mv) * kLog2e);
+        m = mv;
+      }
+      if (m != -INFINITY) {
+        const float mb = m * kLog2e;
+        float t = 0.f;
+        for (int k = 0; k < 8; ++k) t += ex2_approx(fmaf(f[k], kLog2e, -mb));
+        s += t;
+      }
     }
   } else {
-    for (int64_t i = threadIdx.x; i < V; i += kBlock) m = fmaxf(m, load1<BF>(logits, base + i));
+    for (int64_t i = threadIdx.x; i < V; i += kBlock) lse_merge(m, s, load1<BF>(logits, base + i), 1.f);
   }
-  m = block_reduce(m, true, sm);
-  // sweep 2 (L2): sum of exp(x - max)
-  float s = 0.f;
-  if (VEC) {
-    for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
-      float f[8];
-      unpack8<BF>(__ldg(l4 + i), f);
-      for (int k = 0; k < 8; ++k) s += expf(f[k] - m);
-    }
-  } else {
-    for (int64_t i = threadIdx.x; i < V; i += kBlock) s += expf(load1<BF>(logits, base + i) - m);
-  }
-  s = block_reduce(s, false, sm);
+  block_lse(m, s, sm_m, sm_s);
   const float l = m + logf(s);
   if (threadIdx.x == 0) {
     lse_out[row] = l;
@@ -346,7 +368,7 @@ __global__ void __launch_bounds__(kBlock)
     for (int64_t i = threadIdx.x; i < V / 8; i += kBlock) {
       float f[8];
       unpack8<BF>(__ldg(l4 + i), f);
-      for (int k = 0; k < 8; ++k) f[k] = expf(f[k] - l);
+      for (int k = 0; k < 8; ++k) f[k] = ex2_approx(fmaf(f[k], kLog2e, -l * kLog2e));
       p4[i] = pack8<BF>(f);
     }
   } else {

@@ -49,7 +49,8 @@ def test_silu_mul_forward_backward(shape, dtype):
 
 
 @pytest.mark.parametrize("N,D,dtype", [(333, 1024, torch.bfloat16), (17, 100, torch.bfloat16),
-                                       (64, 2048, torch.float16)])
+                                       (64, 2048, torch.float16), (45, 2560, torch.bfloat16),
+                                       (9, 8208, torch.bfloat16)])
 def test_rmsnorm_residual_forward_backward(N, D, dtype):
     from simpletrain_b200.fused_ops import fused_rmsnorm_residual
     g = torch.Generator().manual_seed(1)
