@@ -458,51 +458,70 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           if (D == 128) {
             const int row = Td.row[0];
             constexpr int W = Carry<D>::W;
-            for (int sl = 0; sl < W / 16; ++sl) {  // column slices of 16
-              const int col0 = W * e.cg + 16 * sl;
-              const uint32_t pb = sb + L::SB + (uint32_t)((col0 >> 6) * L::PANEL);
-              uint32_t u32[16], w32[16];
-              if (c == u.c_begin) {
-                if (prev) {
-                  for (int q4 = 0; q4 < 4; ++q4) {
-                    const float4 v = __ldcg(prev + (4 * sl + q4) * kEpi + e.et);
-                    u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
-                    u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
+            // column slices of SW, one tensor-memory round trip each: 32 without the
+            // decay gradient, 16 when W and the tangent come along (register budget)
+            auto slices = [&](auto swc) {
+              constexpr int SW = decltype(swc)::value;
+              for (int sl = 0; sl < W / SW; ++sl) {
+                const int col0 = W * e.cg + SW * sl;
+                const uint32_t pb = sb + L::SB + (uint32_t)((col0 >> 6) * L::PANEL);
+                const uint32_t tz = tmem + e.lane_off + L::A_Z + col0, tw = tmem + e.lane_off + L::A_Y + col0;
+                uint32_t u32[SW], w32[SW];
+                if (c == u.c_begin) {
+                  if (prev) {
+                    for (int q4 = 0; q4 < SW / 4; ++q4) {
+                      const float4 v = __ldcg(prev + ((SW / 4) * sl + q4) * kEpi + e.et);
+                      u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
+                      u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
+                    }
+                  } else if (a.s_in) {
+                    const float4 *s4 = reinterpret_cast<const float4 *>(a.s_in + sbase + (size_t)row * D + col0);
+                    for (int q4 = 0; q4 < SW / 4; ++q4) {
+                      const float4 v = __ldg(s4 + q4);
+                      u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
+                      u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
+                    }
+                  } else {
+                    for (int k = 0; k < SW; ++k) u32[k] = 0u;
                   }
-                } else if (a.s_in) {
-                  const float4 *s4 = reinterpret_cast<const float4 *>(a.s_in + sbase + (size_t)row * D + col0);
-                  for (int q4 = 0; q4 < 4; ++q4) {
-                    const float4 v = __ldg(s4 + q4);
-                    u32[4 * q4] = __float_as_uint(v.x); u32[4 * q4 + 1] = __float_as_uint(v.y);
-                    u32[4 * q4 + 2] = __float_as_uint(v.z); u32[4 * q4 + 3] = __float_as_uint(v.w);
+                  if (want_dd) {
+                    if constexpr (SW == 16) tmem_ld_32x32b_x16(tw, w32);
+                    else tmem_ld_32x32b_x32(tw, w32);
                   }
+                } else if constexpr (SW == 16) {
+                  if (want_dd) tmem_ld2_32x32b_x16(tz, u32, tw, w32);
+                  else tmem_ld_32x32b_x16(tz, u32);
                 } else {
-                  for (int k = 0; k < 16; ++k) u32[k] = 0u;
+                  if (want_dd) {
+                    tmem_ld_32x32b_x32_nowait(tz, u32);
+                    tmem_ld_32x32b_x32_nowait(tw, w32);
+                    tmem_wait_ld_bind(u32, w32);
+                  } else {
+                    tmem_ld_32x32b_x32(tz, u32);
+                  }
                 }
-                if (want_dd) tmem_ld_32x32b_x16(tmem + e.lane_off + L::A_Y + col0, w32);
-              } else if (want_dd) {
-                tmem_ld2_32x32b_x16(tmem + e.lane_off + L::A_Z + col0, u32, tmem + e.lane_off + L::A_Y + col0, w32);
-              } else {
-                tmem_ld_32x32b_x16(tmem + e.lane_off + L::A_Z + col0, u32);
+                if (want_dd) {
+                  float acc = 0.f;
+                  for (int k = 0; k < SW; ++k) acc = fmaf(Td.x[0][SW * sl + k], __uint_as_float(w32[k]), acc);
+                  dl[0] += acc;
+                }
+                for (int j = 0; j < SW / 8; ++j)
+                  st_shared_v4(pb + swz(row, (col0 & 63) + 8 * j),
+                               pack2(sop * __uint_as_float(u32[8 * j]), sop * __uint_as_float(u32[8 * j + 1]), BF),
+                               pack2(sop * __uint_as_float(u32[8 * j + 2]), sop * __uint_as_float(u32[8 * j + 3]), BF),
+                               pack2(sop * __uint_as_float(u32[8 * j + 4]), sop * __uint_as_float(u32[8 * j + 5]), BF),
+                               pack2(sop * __uint_as_float(u32[8 * j + 6]), sop * __uint_as_float(u32[8 * j + 7]), BF));
+                for (int k = 0; k < SW; ++k) {
+                  const float sv = __uint_as_float(u32[k]);
+                  if (!PS && want_dd) Td.x[0][SW * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][SW * sl + k]);
+                  u32[k] = __float_as_uint(stm * sv);
+                }
+                if constexpr (SW == 16) tmem_st_32x32b_x16_nowait(tz, u32);
+                else tmem_st_32x32b_x32_nowait(tz, u32);
               }
-              if (want_dd) {
-                float acc = 0.f;
-                for (int k = 0; k < 16; ++k) acc = fmaf(Td.x[0][16 * sl + k], __uint_as_float(w32[k]), acc);
-                dl[0] += acc;
-              }
-              for (int j = 0; j < 2; ++j)
-                st_shared_v4(pb + swz(row, (col0 & 63) + 8 * j),
-                             pack2(sop * __uint_as_float(u32[8 * j]), sop * __uint_as_float(u32[8 * j + 1]), BF),
-                             pack2(sop * __uint_as_float(u32[8 * j + 2]), sop * __uint_as_float(u32[8 * j + 3]), BF),
-                             pack2(sop * __uint_as_float(u32[8 * j + 4]), sop * __uint_as_float(u32[8 * j + 5]), BF),
-                             pack2(sop * __uint_as_float(u32[8 * j + 6]), sop * __uint_as_float(u32[8 * j + 7]), BF));
-              for (int k = 0; k < 16; ++k) {
-                const float sv = __uint_as_float(u32[k]);
-                if (!PS && want_dd) Td.x[0][16 * sl + k] = alr[0] * fmaf(Lf, sv, Td.x[0][16 * sl + k]);
-                u32[k] = __float_as_uint(stm * sv);
-              }
-              tmem_st_32x32b_x16_nowait(tmem + e.lane_off + L::A_Z + col0, u32);
-            }
+            };
+            if (want_dd) slices(std::integral_constant<int, 16>{});
+            else slices(std::integral_constant<int, 32>{});
             tmem_wait_st();
           } else {
             Carry<D> Sp;
