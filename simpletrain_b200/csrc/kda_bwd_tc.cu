@@ -660,6 +660,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                          const BwdArgs a, const Queue qu) {
   using L = RevLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+  // D=128, chunk-constant decay: dk and dv are accumulated transposed (M = 128 over the
+  // head dimension, N = 64 tokens: full-height tcgen05 tiles instead of M=64 ones) and
+  // written back through transposing stores; literal and per-step keep the M=64 form.
+  constexpr bool TR = !LIT && !PS && D == 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
@@ -726,6 +730,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       const uint32_t id_dki = LIT ? idesc_f16(64, 64, BF, false, true) : idesc_f16(64, D, BF, false, false);
       const uint32_t id_dvi = LIT ? idesc_f16(64, 64, BF, true, true) : idesc_f16(64, D, BF, false, true);
       const uint32_t id_t = idesc_f16(64, D, BF, true, true);  // dP^T Q and P^T dO
+      // transposed dk / dv (TR): M = D over the head dimension, N = 64 tokens
+      const uint32_t id_dkt = idesc_f16(D, 64, BF, false, false);  // dS V^T
+      const uint32_t id_dvt = idesc_f16(D, 64, BF, true, false);   // dS^T K^T
+      const uint32_t id_tt = idesc_f16(D, 64, BF, true, true);     // Q^T dP and dO^T P
       int gc = 0;
       for (int i = 0;; ++i) {
         KDA_TAKE_UNIT(true)
@@ -767,6 +775,14 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
               mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::SB + ks * 2048, L::PANEL),
                       sdesc_mn(st + L::ST_K + ks * 2048, kTile), id_dvi, ks > 0);
             }
+          } else if (TR) {
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
+              const uint32_t poff = (ks >> 2) * L::PANEL + (ks & 3) * 32;
+              mma_f16(tmem + L::A_X, sdesc_k(sb + L::SB + poff), sdesc_k(st + L::ST_V + off), id_dkt, ks > 0);
+              mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::SB + ks * 2048, L::PANEL), sdesc_k(st + L::ST_K + off), id_dvt,
+                      ks > 0);
+            }
           } else {
             for (int ks = 0; ks < D / 16; ++ks) {
               const uint32_t off = (ks >> 2) * kTile + (ks & 3) * 32;
@@ -782,10 +798,17 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
             break;
           tc_fence_after();
           for (int ks = 0; ks < 4; ++ks) {
-            mma_f16(tmem + L::A_X, sdesc_mn(sb + L::DP + ks * 2048, kTile), sdesc_mn(st + L::ST_Q + ks * 2048, kTile),
-                    id_t, 1);
-            mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::P + ks * 2048, kTile), sdesc_mn(st + L::ST_DO + ks * 2048, kTile),
-                    id_t, 1);
+            if (TR) {
+              mma_f16(tmem + L::A_X, sdesc_mn(st + L::ST_Q + ks * 2048, kTile), sdesc_mn(sb + L::DP + ks * 2048, kTile),
+                      id_tt, 1);
+              mma_f16(tmem + L::A_Y, sdesc_mn(st + L::ST_DO + ks * 2048, kTile), sdesc_mn(sb + L::P + ks * 2048, kTile),
+                      id_tt, 1);
+            } else {
+              mma_f16(tmem + L::A_X, sdesc_mn(sb + L::DP + ks * 2048, kTile), sdesc_mn(st + L::ST_Q + ks * 2048, kTile),
+                      id_t, 1);
+              mma_f16(tmem + L::A_Y, sdesc_mn(sb + L::P + ks * 2048, kTile), sdesc_mn(st + L::ST_DO + ks * 2048, kTile),
+                      id_t, 1);
+            }
           }
           mma_commit(bar(DKV_FULL));
           mma_commit(bar(EMPTY + s));
@@ -898,9 +921,15 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (!(ok = mbar_wait(bar(DKV_FULL), ph, a.status, abort_flag))) break;
         if (e.et == 0) KDA_TRACE_EVENT(24, gc);
         tc_fence_after();
-        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, sb + L::DK, 0, false, rk);
-        if (e.et == 0) KDA_TRACE_EVENT(25, gc);
-        frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_Y, sb + L::DV, 0, false);
+        if constexpr (TR) {
+          tile_from_transposed<BF>(e, tmem, L::A_X, sb + L::DK);
+          if (e.et == 0) KDA_TRACE_EVENT(25, gc);
+          tile_from_transposed<BF>(e, tmem, L::A_Y, sb + L::DV);
+        } else {
+          frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_X, sb + L::DK, 0, false, rk);
+          if (e.et == 0) KDA_TRACE_EVENT(25, gc);
+          frag_to_tile<D, BF>(e, tmem + e.lane_off + L::A_Y, sb + L::DV, 0, false);
+        }
         tc_fence_before();
         mbar_arrive(bar(DKV_FREE));
         fence_async_smem();

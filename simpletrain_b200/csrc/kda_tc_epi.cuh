@@ -314,6 +314,36 @@ __device__ __forceinline__ void frag_to_tile(const Epi &e, uint32_t taddr, uint3
     }
 }
 
+// 8x8 16-bit matrices stored transposed from the mma fragment layout (thread t
+// holds row t/4, columns 2(t%4) and 2(t%4)+1 of each); thread t gives the
+// address of stored row t%8 of matrix t/8 (16 bytes, 16-byte aligned).
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0),
+               "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+
+// M=128, N=64 accumulator (tensor-memory lane = row m, column n) at column base
+// `acc` -> the 16-bit tile of its transpose, [64 rows n x 128 columns m] in two
+// swizzled boxes.  Warp (sp, cg) converts lanes 32 sp .. 32 sp + 31 and columns
+// 32 cg .. 32 cg + 31: 16x256b loads deliver the 8x8 fragment layout, which
+// stmatrix .trans writes out as 16-byte runs of 8 consecutive m for one n.
+template <bool BF>
+__device__ __forceinline__ void tile_from_transposed(const Epi &e, uint32_t tmem, uint32_t acc, uint32_t tile) {
+  const int mat = e.lane >> 3, rho = e.lane & 7;
+  for (int hh = 0; hh < 2; ++hh) {  // the two 16-lane halves of this warp's lanes
+    uint32_t r[16];  // value (row half ee, column block j, k) at r[4 j + 2 ee + k]
+    tmem_ld_16x256b_x4(tmem + e.lane_off + ((uint32_t)(16 * hh) << 16) + acc + 32 * e.cg, r);
+    for (int k = 0; k < 4; k += 2) {  // matrices (ee, k), (ee, k + 1) for ee = 0, 1
+      const int ee = mat & 1, kk = k + (mat >> 1);
+      const int m0 = 32 * e.sp + 16 * hh + 8 * ee, n = 32 * e.cg + 8 * kk + rho;
+      const uint32_t addr = tile + (uint32_t)((m0 >> 6) * kTile) + swz(n, m0 & 63);
+      auto pk = [&](int i) { return pack2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), BF); };
+      stmatrix_x4_trans(addr, pk(4 * k), pk(4 * k + 2), pk(4 * (k + 1)), pk(4 * (k + 1) + 2));
+    }
+  }
+}
+
 // ------------------------------------------------------ per-step decay --
 // Per-step semantics (one decay a per stream, s_t = a s_{t-1} + k_t^T v_t)
 // run on the chunk kernels with a row-scaled k tile,
