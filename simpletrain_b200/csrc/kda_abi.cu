@@ -127,7 +127,8 @@ size_t queue_bytes(int nranges, int slot_f4) {
 
 // Whether some range lies strictly inside one stream (starts and ends
 // mid-stream): then the carry would pass through a chain of ranges, and the
-// ranges' aggregates are precomputed so each link costs only a combine.
+// aggregates of every publishing piece are precomputed so each link costs
+// only a combine.
 bool has_middle(int nstreams, int nchunks, int nranges) {
   if (nchunks <= 0 || nranges <= 0) return false;
   const long long n = (long long)nstreams * nchunks;
@@ -139,7 +140,7 @@ bool has_middle(int nstreams, int nchunks, int nranges) {
   return false;
 }
 
-// aggregate buffer of one queue: nranges x agg_f4 x 256 float4 (only with middle ranges)
+// aggregate buffer of one queue: nranges x agg_f4 x 256 float4 (only when some range is a middle range)
 size_t agg_bytes(int nstreams, int nchunks, int nranges, int agg_f4) {
   return has_middle(nstreams, nchunks, nranges) ? (size_t)nranges * agg_f4 * kda::tc::kEpi * 16 : 0;
 }
@@ -200,7 +201,7 @@ size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32
   const int nc = n_chunks(T, chunk), nr = n_ranges(B * H, nc, bwd_slots());
   // forward-direction pass: state, decay tangent, decay-gradient share; reverse pass: dS;
   // then dO = dy * g, [B][H][T][D] 16-bit, handed from the first pass to the second;
-  // then the middle-range aggregates of both passes
+  // then the range aggregates of both passes (long streams)
   return queue_bytes(nr, 2 * carry_f4(D) + 1) + queue_bytes(nr, carry_f4(D)) + do_bytes(B, H, T, D) +
          agg_bytes(B * H, nc, nr, 2 * carry_f4(D)) + agg_bytes(B * H, nc, nr, carry_f4(D));
 }

@@ -1,19 +1,21 @@
 // Range aggregates for long streams (sm_100a, tcgen05 + TMEM + TMA).
 //
-// When a (batch, head) stream is longer than one work range, the ranges in
-// its middle both wait for an entry carry and publish an exit carry.  The
-// carry recurrences are linear with a diagonal (per key channel) decay, so a
-// middle range's exit carry is
+// When (batch, head) streams are longer than a work range, a chain of ranges
+// hands the carry along each stream.  The carry recurrences are linear with a
+// diagonal (per key channel) decay, so the exit carry of a range's publishing
+// piece (a middle range, or the piece that starts -- reverse: ends -- a
+// stream, whose entry is the initial carry) is
 //
 //   S_out = A S_in + S_loc,         A = decay^(64 n)   (n full chunks)
 //   T_out = A T_in + 64 n A S_in + T_loc               (decay tangent)
 //   dS_out = A dS_in + dS_loc                          (reverse pass)
 //
 // where the _loc terms are the same recurrences run from zero over the
-// range's chunks.  This kernel computes them for every middle range (one CTA
-// per range, all in parallel), so the main kernels can publish a middle
-// range's exit carry as soon as its entry carry arrives instead of after the
-// range's full work (kernels/kda_kernel.py:292-295 is the recurrence).
+// piece's chunks.  This kernel computes them for every range (one CTA per
+// range, all in parallel), so the main kernels publish each exit carry as soon
+// as the entry carry is known instead of after the piece's full work, and no
+// range waits for a whole chain of earlier ones (kernels/kda_kernel.py:292-295
+// is the recurrence).
 //
 //   MODE 0  S_loc from K, V            (forward)
 //   MODE 1  S_loc, T_loc from K, V     (backward, forward direction)
@@ -64,10 +66,13 @@ __global__ void __launch_bounds__(kThreads + (agg_scales<PS, MODE>() ? 32 : 0), 
   using L = AggLayout<D, NS>;
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   constexpr bool REV = MODE == 2;
-  // this CTA's range; only middle ranges (one piece, both ends mid-stream) have work
+  // this CTA's range: the aggregate of the piece through which it publishes a carry
+  // (reverse: a piece that ends at its stream's end starts with the ragged last chunk,
+  // whose own decay factor multiplies a zero carry here and enters the consumer's A)
   const Span sp = span_of(qu, REV ? qu.nranges - 1 - (int)blockIdx.x : (int)blockIdx.x, REV);
-  if (sp.npieces() != 1 || sp.c0 == 0 || sp.c1 == qu.nchunks) return;
-  const int stream = sp.s0, c_begin = sp.c0, c_end = sp.c1, n = c_end - c_begin;
+  int stream, c_begin, c_end;
+  if (!published_piece(qu, sp, REV, stream, c_begin, c_end)) return;
+  const int n = c_end - c_begin;
   const int b = stream / a.H, h = stream - b * a.H;
 
   extern __shared__ uint8_t smem_raw[];

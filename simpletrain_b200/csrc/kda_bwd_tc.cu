@@ -365,8 +365,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       }
       const bool early = u.early(qu);
       if (early) {
-        // middle range: exit state and tangent follow from the entry ones and the aggregate:
+        // exit state and tangent follow from the entry ones (the boundary slot, or at a
+        // stream start the initial state and a zero tangent) and the aggregate:
         // S_out = A S_in + S_loc, T_out = A T_in + 64 n A S_in + T_loc
+        const float *sin = a.s_in ? a.s_in + sbase : nullptr;
         const int n = u.c_end - u.c_begin;
         float A[Carry<D>::NR], An[Carry<D>::NR];
         for (int r = 0; r < Carry<D>::NR; ++r) {
@@ -378,7 +380,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         const float *ft = &Td.x[0][0];
         for (int i4 = 0; i4 < CF4; ++i4) {  // one float4 of S and of T at a time
           const int r = (4 * i4) / Carry<D>::NV;
-          const float4 sv = __ldcg(prev + i4 * kEpi + e.et);
+          const float4 sv = prev ? __ldcg(prev + i4 * kEpi + e.et)
+                                 : sin ? Td.rm_f4(e, sin, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
           const float4 gs = __ldcg(ag + i4 * kEpi + e.et);
           if constexpr (PS) {  // no tangent without a decay gradient
             __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
@@ -850,9 +853,12 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       }
       const bool early = u.early(qu);
       if (early) {
-        // middle range: dS at its start follows from dS at its end and the aggregate
+        // dS at the piece's start follows from dS at its end and the aggregate; a piece
+        // that ends its stream includes the ragged last chunk (decay^Ltail)
+        const int n = u.c_end - u.c_begin;
+        const bool tail = u.c_end == qu.nchunks;
         float A[Carry<D>::NR];
-        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
+        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
         combine_store<D>(e, dS, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
         chain_publish(e, qu, u.pub_slot);
       }
@@ -984,7 +990,7 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L2::SMEM);
   if (e != cudaSuccess) return e;
   const int dtype = BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16;
-  if (q1.agg) {  // middle ranges: state (and tangent) aggregates from k, v
+  if (q1.agg) {  // long streams: state (and tangent) aggregates from k, v
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q1.agg, q1.agg_f4, a.status};
     if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, st)) != cudaSuccess) return e;
   }
@@ -992,7 +998,7 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (q2.agg) {  // middle ranges: dS aggregates from q and the dO the first pass wrote
+  if (q2.agg) {  // long streams: dS aggregates from q and the dO the first pass wrote
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q2.agg, q2.agg_f4, a.status};
     if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, st)) != cudaSuccess) return e;
   }

@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
       }
       const bool early = u.early(qu);
       if (early) {
-        // middle range: its exit state follows from the entry state and its aggregate
+        // the exit state follows from the entry state (slot or initial state) and the aggregate
         float A[Carry<D>::NR];
         for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
         combine_store<D>(e, S, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
@@ -492,7 +492,7 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
   auto kern = fwd_tc_kernel<T, D, LIT, PS, NS, NY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  if (q.agg) {  // middle ranges: their state aggregates first
+  if (q.agg) {  // long streams: the state aggregates first
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q.agg, q.agg_f4, a.status};
     e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, st);
     if (e != cudaSuccess) return e;

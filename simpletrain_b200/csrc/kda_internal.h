@@ -69,8 +69,9 @@ namespace tc {
 struct Queue;
 }
 
-// Range aggregates (kda_agg_tc.cu): the carry recurrence of each middle range
-// run from zero, stored thread-major at agg + r * agg_f4 * 256 float4.
+// Range aggregates (kda_agg_tc.cu): the carry recurrence over the publishing
+// piece of each range run from zero, stored thread-major at
+// agg + r * agg_f4 * 256 float4.
 struct AggArgs {
   int B, H, T, D;
   int literal;

@@ -153,6 +153,18 @@ struct Carry {
         }
     }
   }
+  // float4 number i4 of this thread's registers (the slot order), read straight
+  // from a row-major [D][D] state instead of being held in registers
+  __device__ float4 rm_f4(const Epi &e, const float *src, int i4) const {
+    const int r = (4 * i4) / NV, i = (4 * i4) % NV;
+    if constexpr (D == 128) {
+      return __ldg(reinterpret_cast<const float4 *>(src + (size_t)row[0] * D + W * e.cg + i));
+    } else {
+      const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + (size_t)row[r] * D + col(e, i)));
+      const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + (size_t)row[r] * D + col(e, i + 2)));
+      return make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+  }
   __device__ void store_rm(const Epi &e, float *dst) const {
     if constexpr (D == 128) {
       float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)row[0] * D + W * e.cg);
@@ -411,7 +423,7 @@ struct Queue {
   float4 *slots;   // [nranges + 1][slot_f4 * kEpi]: carried state at range boundary r
   int slot_f4;     // float4 per thread per slot
   int nstreams, nchunks, nranges;
-  float4 *agg;     // [nranges][agg_f4 * kEpi]: middle-range aggregates, or null
+  float4 *agg;     // [nranges][agg_f4 * kEpi]: aggregates of the publishing pieces, or null
   int agg_f4;
 };
 
@@ -420,11 +432,10 @@ struct Piece {
   int wait_slot;               // boundary slot holding the entry state, or -1 (stream end / start)
   int pub_slot;                // boundary slot for the exit state, or -1
   int range;
-  // a middle range (one piece, both ends mid-stream) with a precomputed
-  // aggregate publishes its exit state as soon as its entry state is known
-  __device__ __forceinline__ bool early(const Queue &qu) const {
-    return wait_slot >= 0 && pub_slot >= 0 && qu.agg != nullptr;
-  }
+  // with precomputed aggregates (long streams), a piece that publishes does so
+  // as soon as its entry state is known: from the boundary slot, or at the
+  // start of its stream the initial state
+  __device__ __forceinline__ bool early(const Queue &qu) const { return pub_slot >= 0 && qu.agg != nullptr; }
 };
 
 // Range of ticket t: stream-major positions [N t / R, N (t+1) / R), N = streams x chunks.
@@ -461,6 +472,26 @@ __device__ __forceinline__ Piece piece_of(const Queue &qu, const Span &sp, int p
   pc.pub_slot = reverse ? at_begin : at_end;
   pc.range = sp.r;
   return pc;
+}
+
+// The piece of a range that publishes a carry (forward: the last piece, when it
+// ends mid-stream; reverse: the first, when it starts mid-stream) as its stream
+// and chunks [cb, ce); false when the range publishes nothing.  Its aggregate
+// is stored at the range's index.
+__device__ __forceinline__ bool published_piece(const Queue &qu, const Span &sp, bool reverse, int &s, int &cb,
+                                                int &ce) {
+  if (!reverse) {
+    if (sp.c1 == qu.nchunks) return false;
+    s = sp.s1;
+    cb = sp.npieces() == 1 ? sp.c0 : 0;
+    ce = sp.c1;
+  } else {
+    if (sp.c0 == 0) return false;
+    s = sp.s0;
+    cb = sp.c0;
+    ce = sp.npieces() == 1 ? sp.c1 : qu.nchunks;
+  }
+  return true;
 }
 
 __device__ __forceinline__ float4 *slot_ptr(const Queue &qu, int slot) {
@@ -513,8 +544,9 @@ __device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int
   }
 }
 
-// Exit carry of a middle range from its entry carry x and its aggregate:
-// out = A x + agg (A = decay^(64 n) per row), stored thread-major like a slot.
+// Exit carry of a publishing piece from its entry carry x and its aggregate:
+// out = A x + agg (A = the product of the piece's chunk decays per row),
+// stored thread-major like a slot.
 template <int D>
 __device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, const float (&A)[Carry<D>::NR],
                                               const float4 *agg, float4 *dst) {
