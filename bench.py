@@ -88,6 +88,11 @@ class ClockSampler:
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
+            # nvidia-smi takes a moment to start: wait (at most 3 s) for its first
+            # sample so that even a short timed region is covered
+            t0 = time.time()
+            while os.path.getsize(self.path) == 0 and self.proc.poll() is None and time.time() - t0 < 3.0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -270,49 +275,37 @@ def run_ours(args, w, rank, world, local_rank):
 
 
 def run_e2e(args, w, rank, world, dev, inp):
-    """Same metric through the public API (kda_chunk + autograd) with pinned host
-    buffers: each step copies its inputs host->device and its outputs
-    (y, dq, dk, dv, dg, d_decay) device->host inside the timed region."""
+    """Same metric through the public host-buffer API (``HostScan``): each step
+    copies its inputs (q, k, v, g, dy, decay, initial state) from pinned host
+    memory to the device and its results (y, final state, dq, dk, dv, dg,
+    d_decay, d_initial_state) back, inside the timed region; the batch is
+    pipelined in slices so both copy directions overlap the kernels."""
     import torch.distributed as dist
 
-    from simpletrain_b200 import kda_chunk
+    from simpletrain_b200.host_stream import HostScan
 
     names = ["q", "k", "v", "g", "dy"] if w.backward else ["q", "k", "v", "g"]
 
     def pinned_like(t):
         return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device="cpu", pin_memory=True)
 
-    host = {n: pinned_like(inp[n]) for n in names + ["decay"]}
-    for n in names + ["decay"]:
+    extra = ["decay"] + (["s0"] if inp["s0"] is not None else [])
+    host = {n: pinned_like(inp[n]) for n in names + extra}
+    for n in names + extra:
         host[n].copy_(inp[n])
-    outs = None
-    dev_in = {n: torch.empty_like(inp[n]) for n in names + ["decay"]}
+    # per-step: one decay per head (the first channel's), not differentiated
+    decay = host["decay"][:, 0].contiguous() if args.per_step else host["decay"]
+    scan = HostScan(dev, slices=args.e2e_slices, chunk_size=w.chunk, per_step=args.per_step)
     steps = args.e2e_steps
-    h2d = sum(host[n].numel() * host[n].element_size() for n in names + ["decay"])
+    h2d = sum(host[n].numel() * host[n].element_size() for n in names + ["s0"] if n in host)
+    h2d += decay.numel() * decay.element_size()
     d2h = 0
 
     def one():
-        nonlocal outs, d2h
-        for n in names + ["decay"]:
-            dev_in[n].copy_(host[n], non_blocking=True)
-        if args.per_step:  # one decay per head, not differentiated
-            leaves = [dev_in[n].requires_grad_(w.backward) for n in ("q", "k", "v", "g")]
-            y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], dev_in["decay"][:, 0], inp["s0"],
-                             per_step=True)
-        else:
-            leaves = [dev_in[n].requires_grad_(w.backward) for n in ("q", "k", "v", "g", "decay")]
-            y, S = kda_chunk(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], inp["s0"])
-        if w.backward:
-            res = [y] + list(torch.autograd.grad([y], leaves, [dev_in["dy"]]))
-        else:
-            res = [y]
-        if outs is None:
-            outs = [pinned_like(r) for r in res]
-            d2h = sum(o.numel() * o.element_size() for o in outs)
-        for o, r in zip(outs, res):
-            o.copy_(r, non_blocking=True)
-        for n in names + ["decay"]:
-            dev_in[n] = dev_in[n].detach()
+        nonlocal d2h
+        out = scan(host["q"], host["k"], host["v"], host["g"], decay, dy=host.get("dy"),
+                   initial_state=host.get("s0"))
+        d2h = sum(o.numel() * o.element_size() for o in out.values())
 
     for _ in range(2):
         one()
@@ -333,7 +326,9 @@ def run_e2e(args, w, rank, world, dev, inp):
     ms = float(t.item())
     return {"value": round(world * w.B * w.T * steps / (ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "api": "simpletrain_b200.kda_chunk + torch.autograd.grad, pinned host buffers"}
+            "slices": scan.slices if scan.slices is not None else min(w.B, 16),
+            "api": "simpletrain_b200.host_stream.HostScan (pinned host buffers, batch slices pipelined "
+                   "over copy-in / scan / copy-out streams)"}
 
 
 # --------------------------------------------------------------------------- #
@@ -550,6 +545,8 @@ def main():
                     help="per-token decay semantics (one decay per head) instead of chunk-constant decay")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-slices", type=int, default=None,
+                    help="batch slices of the host-buffer pipeline (default min(B, 16))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--fused-ops", action="store_true",

@@ -1,0 +1,203 @@
+"""The KDA scan over host-resident tensors, streamed through one B200.
+
+The reference's CPU path takes host tensors and returns host tensors
+(``kda_chunked_scan(..., use_triton=False)``, kernels/kda_kernel.py:244-297
+and :303-328).  ``HostScan`` gives callers whose q/k/v/g (and dy) live in host
+memory the same call on the GPU without paying the PCIe transfers one after
+the other: it cuts the batch into slices of whole batch rows and runs every
+slice through three CUDA streams -- copy in, scan (forward, and the backward
+when ``dy`` is given), copy out -- so the host-to-device copy of slice i+1,
+the kernels of slice i and the device-to-host copy of slice i-1 run at the
+same time, and the two PCIe directions overlap each other.
+
+Batch rows are independent (b, h) streams of the scan, so a slice needs no
+carry from another slice; the decay gradient of a decay shared over the
+batch is summed over all rows on the device before it is copied back.
+
+Host tensors should be pinned (``pin_memory=True``): copies from pageable
+memory are staged by the driver and overlap nothing.  Device buffers and the
+pinned result buffers are kept for the next call with the same shapes; the
+returned tensors are those buffers, valid until the next call (clone them to
+keep them).  One call at a time per object.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Union
+
+import torch
+from torch import Tensor
+
+from .ops import MODE_CORRECTED, MODE_LITERAL, MODE_PER_STEP, decay_as_bhd, per_step_decay
+
+__all__ = ["HostScan"]
+
+_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def _pinned_like(t: Tensor) -> Tensor:
+    return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device="cpu", pin_memory=True)
+
+
+class HostScan:
+    """KDA chunked scan (forward, optionally backward) of host tensors on one GPU.
+
+    ``HostScan(device=None, slices=None, chunk_size=64, per_step=False,
+    reference_exact=False)``; ``slices`` defaults to ``min(B, 16)`` batch
+    slices (on the 1b shape, B=16, fwd+bwd: 4 slices 2.68 M, 8 slices 2.84 M,
+    16 slices 2.96 M tokens/s).  Calling it with q, k, v (``[B, H, T, D]``
+    bf16/fp16 host tensors, any strides with the batch dimension outermost in
+    memory, such as the
+    ``[B, T, H, D]``-memory views the KDA layer produces), an optional gate,
+    the decay (float or tensor, as for ``kda_chunk``), an optional ``dy`` and
+    initial state returns a dict of host tensors: ``y`` and ``final_state``;
+    with ``dy`` also ``dq``, ``dk``, ``dv``, ``dg`` (with a gate), ``ddecay``
+    (a tensor decay, not per-step) and ``ds0`` (with an initial state) -- the
+    gradients of ``sum(y * dy)``.
+    """
+
+    def __init__(self, device: Optional[Union[int, str, torch.device]] = None, slices: Optional[int] = None,
+                 chunk_size: int = 64, per_step: bool = False, reference_exact: bool = False):
+        if per_step and reference_exact:
+            raise ValueError("per_step and reference_exact are different semantics; pick one")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("HostScan streams host tensors through a CUDA device")
+        self.slices = slices
+        self.chunk = int(chunk_size)
+        self.mode = MODE_PER_STEP if per_step else (MODE_LITERAL if reference_exact else MODE_CORRECTED)
+        self.per_step = per_step
+        self._key = None
+        self._streams = None
+
+    # ------------------------------------------------------------------ #
+    def _buffers(self, key, tensors: Dict[str, Tensor], outs: Dict[str, tuple]):
+        """(Re)allocate device inputs and pinned host results for a new shape."""
+        if key == self._key:
+            return
+        self.dev_in = {n: torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=self.device)
+                       for n, t in tensors.items()}
+        self.host_out = {}
+        for n, (like, shape) in outs.items():
+            if like is not None:
+                self.host_out[n] = _pinned_like(like)
+            else:
+                self.host_out[n] = torch.empty(shape, dtype=torch.float32, pin_memory=True)
+        self._key = key
+
+    def __call__(self, q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
+                 decay: Union[float, Tensor] = 0.99, dy: Optional[Tensor] = None,
+                 initial_state: Optional[Tensor] = None, output_final_state: bool = True) -> Dict[str, Tensor]:
+        if q.dim() != 4:
+            raise ValueError(f"q must be [B, H, T, D], got shape {tuple(q.shape)}")
+        if q.dtype not in _DTYPES:
+            raise TypeError(f"KDA sm_100a kernels take bf16/fp16 inputs, got {q.dtype}")
+        B, H, T, D = q.shape
+        named = {"q": q, "k": k, "v": v}
+        if g is not None:
+            named["g"] = g
+        if dy is not None:
+            named["dy"] = dy
+        for n, t in named.items():
+            if t.device.type != "cpu":
+                raise ValueError(f"HostScan takes host tensors; {n} is on {t.device}")
+            if t.shape != q.shape or t.dtype != q.dtype:
+                raise ValueError(f"{n} must match q's shape {tuple(q.shape)} and dtype {q.dtype}")
+            if t.stride(0) != max(t.stride()) and B > 1:
+                raise ValueError(f"{n}: the batch dimension must be outermost in memory")
+        if initial_state is not None:
+            if initial_state.shape != (B, H, D, D) or initial_state.device.type != "cpu":
+                raise ValueError(f"initial_state must be a host [B, H, D, D] = {(B, H, D, D)} tensor")
+            named["s0"] = initial_state.float()
+        backward = dy is not None
+        dec_t = decay if torch.is_tensor(decay) else None
+        want_dd = backward and dec_t is not None and not self.per_step
+        want_ds0 = backward and initial_state is not None
+
+        outs = {"y": (q, None)}
+        if output_final_state:
+            outs["final_state"] = (None, (B, H, D, D))
+        if backward:
+            outs.update(dq=(q, None), dk=(q, None), dv=(q, None))
+            if g is not None:
+                outs["dg"] = (q, None)
+            if want_dd:
+                outs["ddecay"] = (None, tuple(dec_t.shape))
+            if want_ds0:
+                outs["ds0"] = (None, (B, H, D, D))
+        key = (tuple(q.shape), q.dtype, tuple((n, t.stride()) for n, t in named.items()),
+               tuple(outs), None if dec_t is None else tuple(dec_t.shape))
+        self._buffers(key, named, outs)
+        dev = self.device
+        if self._streams is None:
+            self._streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
+        s_in, s_run, s_out = self._streams
+        caller = torch.cuda.current_stream(dev)
+
+        # the decay, whole, on the device first (small); its [B, H, D] view is sliced per slice
+        with torch.cuda.stream(s_run):
+            s_run.wait_stream(caller)
+            dd = dec_t.to(dev, non_blocking=True) if dec_t is not None else decay
+            if self.per_step:
+                dview, dscal = per_step_decay(dd, B, H, D, q.dtype)
+            else:
+                dview, dscal = decay_as_bhd(dd, B, H, D)
+            dd_rows = torch.empty((B, H, D), dtype=torch.float32, device=dev) if want_dd else None
+        s_in.wait_stream(caller)
+
+        n_sl = max(1, min(B, self.slices if self.slices is not None else 16))
+        bounds = [(B * i // n_sl, B * (i + 1) // n_sl) for i in range(n_sl)]
+        di, ho = self.dev_in, self.host_out
+        for b0, b1 in bounds:
+            if b1 == b0:
+                continue
+            # copy in
+            with torch.cuda.stream(s_in):
+                for n, t in named.items():
+                    di[n][b0:b1].copy_(t[b0:b1], non_blocking=True)
+                arrived = torch.cuda.Event()
+                arrived.record(s_in)
+            # scan
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(arrived)
+                sl = {n: t[b0:b1] for n, t in di.items()}
+                dv_sl = dview[b0:b1] if dview is not None else None
+                s0 = sl.get("s0")
+                y, sT = torch.ops.kda_b200.chunk_fwd(sl["q"], sl["k"], sl["v"], sl.get("g"), dv_sl, dscal, s0,
+                                                      self.chunk, self.mode, bool(output_final_state))
+                res = {"y": y}
+                if output_final_state:
+                    res["final_state"] = sT
+                if backward:
+                    gq, gk, gv, gg, gd, gs0 = torch.ops.kda_b200.chunk_bwd(
+                        sl["q"], sl["k"], sl["v"], sl.get("g"), sl["dy"], dv_sl, dscal, s0, None, None,
+                        self.chunk, self.mode, want_dd, want_ds0)
+                    res.update(dq=gq, dk=gk, dv=gv)
+                    if g is not None:
+                        res["dg"] = gg
+                    if want_dd:
+                        dd_rows[b0:b1].copy_(gd)
+                    if want_ds0:
+                        res["ds0"] = gs0
+                done = torch.cuda.Event()
+                done.record(s_run)
+            # copy out
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for n, t in res.items():
+                    t.record_stream(s_out)
+                    ho[n][b0:b1].copy_(t, non_blocking=True)
+        if want_dd:
+            with torch.cuda.stream(s_run):
+                # d(decay) of the broadcast decay: summed over the rows it was broadcast to
+                d = dec_t.reshape(H, 1) if dec_t.dim() == 1 and dec_t.shape[0] == H else dec_t
+                red = dd_rows.sum_to_size(d.shape).reshape(dec_t.shape)
+                done = torch.cuda.Event()
+                done.record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                red.record_stream(s_out)
+                ho["ddecay"].copy_(red, non_blocking=True)
+        for s in (s_in, s_run, s_out):
+            caller.wait_stream(s)
+        caller.synchronize()
+        return dict(ho)
