@@ -340,6 +340,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
       if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      if (e.et == 0 && i < 2) {
+        KDA_TRACE_CTA(3 + 2 * i, kda_globaltimer());
+        if (i == 0) KDA_TRACE_CTA(1, t);
+      }
       const float4 *prev = u.wait_slot >= 0 ? slot_ptr(qu, u.wait_slot) : nullptr;
       constexpr int CF4 = Carry<D>::FLOATS / 4;  // float4 per thread of one carry
       // the previous range's decay-gradient share is added at the end of the piece
@@ -589,6 +593,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (e.et == 0) KDA_TRACE_EVENT(12, gc);
       }
       if (!ok) break;
+      if (e.et == 0 && i < 2) KDA_TRACE_CTA(4 + 2 * i, kda_globaltimer());
       // piece end: the last K^T V has landed in tensor memory
       if (!mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag)) break;
       tc_fence_after();
