@@ -94,10 +94,19 @@ int ranges_override() {
   return v;
 }
 
-// Ranges of one launch: one per resident CTA slot, at most one per chunk.
+// Ranges of one launch: one per resident CTA slot, at most one per chunk.  With
+// fewer streams than slots but at least half as many, one range per stream
+// instead: cutting streams there puts ranges inside streams, whose carries then
+// need the range aggregates (a pass over k and v before the main kernel), and
+// that costs more than the idle slots.  Measured on 148 slots, forward /
+// backward: 128 streams of 32 chunks (D=128) 105 / 294 us cut, 68 / 226 us one
+// per stream; 96 streams 83 / 237 against 65 / 217; 64 streams of 64 chunks
+// 120 / 329 against 116 / 410, where cutting wins.
 int n_ranges(int nstreams, int nchunks, int slots) {
   const long long n = (long long)nstreams * nchunks;
-  const int want = ranges_override() > 0 ? ranges_override() : slots;
+  int want = slots;
+  if (ranges_override() > 0) want = ranges_override();
+  else if (nstreams < slots && 2LL * nstreams >= slots) want = nstreams;
   return (int)(n < want ? n : want);
 }
 
