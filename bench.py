@@ -165,6 +165,11 @@ def run_ours(args, w, rank, world, local_rank):
     fwd = torch.ops.kda_b200.chunk_fwd
     bwd = torch.ops.kda_b200.chunk_bwd
 
+    # the ops are called directly (their backward explicitly): no autograd
+    # bookkeeping, which would add a Python layer to every call
+    inference = torch.inference_mode()
+    inference.__enter__()
+
     def step():
         y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, mode, True)
         if w.backward:
@@ -219,6 +224,7 @@ def run_ours(args, w, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
+    inference.__exit__(None, None, None)
     status = device_status(dev)
     if status:
         raise RuntimeError(f"device-side KDA status {status}")

@@ -126,7 +126,12 @@ class HostScan:
                 outs["ds0"] = (None, (B, H, D, D))
         key = (tuple(q.shape), q.dtype, tuple((n, t.stride()) for n, t in named.items()),
                tuple(outs), None if dec_t is None else tuple(dec_t.shape))
-        self._buffers(key, named, outs)
+        self._buffers(key, named, outs)  # outside inference mode: the results are ordinary tensors
+        with torch.inference_mode():  # the ops are called directly: no autograd layer per call
+            return self._run(named, q, g, decay, dec_t, backward, want_dd, want_ds0, output_final_state)
+
+    def _run(self, named, q, g, decay, dec_t, backward, want_dd, want_ds0, output_final_state):
+        B, H, T, D = q.shape
         dev = self.device
         if self._streams is None:
             self._streams = [torch.cuda.Stream(device=dev) for _ in range(3)]

@@ -109,6 +109,7 @@ def test_host_scan_reuses_buffers_and_new_shapes():
     assert b["y"].data_ptr() == ptr
     for n in ref:
         assert torch.equal(b[n], ref[n]), n   # same inputs, same slices: identical
+    b["dq"].add_(1)   # ordinary tensors: in-place use outside inference mode works
     q2, k2, v2, g2, dy2, _ = _inputs(3, 2, 64, 64, seed=25)
     c = scan(q2, k2, v2, g2, 0.9, dy=dy2)
     _check(c, _device_reference(q2, k2, v2, g2, 0.9, dy2, None))
