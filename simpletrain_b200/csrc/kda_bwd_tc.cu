@@ -382,24 +382,31 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         const float4 *ag = agg_ptr(qu, u.range);
         float4 *dst = slot_ptr(qu, u.pub_slot);
         const float *ft = &Td.x[0][0];
-        for (int i4 = 0; i4 < CF4; ++i4) {  // one float4 of S and of T at a time
-          const int r = (4 * i4) / Carry<D>::NV;
-          const float4 sv = prev ? __ldcg(prev + i4 * kEpi + e.et)
-                                 : sin ? Td.rm_f4(e, sin, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 gs = __ldcg(ag + i4 * kEpi + e.et);
-          if constexpr (PS) {  // no tangent without a decay gradient
-            __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
-                                                       fmaf(A[r], sv.z, gs.z), fmaf(A[r], sv.w, gs.w)));
-            continue;
+        // batches of float4 of S and of T; each batch's loads go out before its
+        // stores (a store between loads would make every load its own round trip)
+        constexpr int BATCH = CF4 < 2 ? CF4 : 2;
+        for (int i0 = 0; i0 < CF4; i0 += BATCH) {
+          float4 sv[BATCH], gs[BATCH], gt[BATCH];
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int i4 = i0 + j;
+            sv[j] = prev ? __ldcg(prev + i4 * kEpi + e.et)
+                         : sin ? Td.rm_f4(e, sin, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            gs[j] = __ldcg(ag + i4 * kEpi + e.et);
+            if constexpr (!PS) gt[j] = __ldcg(ag + (CF4 + i4) * kEpi + e.et);  // no tangent in per-step mode
           }
-          const float4 gt = __ldcg(ag + (CF4 + i4) * kEpi + e.et);
-          __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv.x, gs.x), fmaf(A[r], sv.y, gs.y),
-                                                     fmaf(A[r], sv.z, gs.z), fmaf(A[r], sv.w, gs.w)));
-          __stcg(dst + (CF4 + i4) * kEpi + e.et,
-                 make_float4(fmaf(A[r], ft[4 * i4], fmaf(An[r], sv.x, gt.x)),
-                             fmaf(A[r], ft[4 * i4 + 1], fmaf(An[r], sv.y, gt.y)),
-                             fmaf(A[r], ft[4 * i4 + 2], fmaf(An[r], sv.z, gt.z)),
-                             fmaf(A[r], ft[4 * i4 + 3], fmaf(An[r], sv.w, gt.w))));
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int i4 = i0 + j, r = (4 * i4) / Carry<D>::NV;
+            __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv[j].x, gs[j].x), fmaf(A[r], sv[j].y, gs[j].y),
+                                                       fmaf(A[r], sv[j].z, gs[j].z), fmaf(A[r], sv[j].w, gs[j].w)));
+            if constexpr (!PS)
+              __stcg(dst + (CF4 + i4) * kEpi + e.et,
+                     make_float4(fmaf(A[r], ft[4 * i4], fmaf(An[r], sv[j].x, gt[j].x)),
+                                 fmaf(A[r], ft[4 * i4 + 1], fmaf(An[r], sv[j].y, gt[j].y)),
+                                 fmaf(A[r], ft[4 * i4 + 2], fmaf(An[r], sv[j].z, gt[j].z)),
+                                 fmaf(A[r], ft[4 * i4 + 3], fmaf(An[r], sv[j].w, gt[j].w))));
+          }
         }
         chain_publish(e, qu, u.pub_slot, 1);
       }

@@ -298,6 +298,10 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
       if (e.et == 0) KDA_TRACE_EVENT(15, gc);
       if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       if (e.et == 0) KDA_TRACE_EVENT(16, gc);
+      if (e.et == 0 && i == 0) {
+        KDA_TRACE_CTA(4, kda_globaltimer());
+        KDA_TRACE_CTA(6, t);
+      }
       if (u.wait_slot < 0) S.load_rm(e, a.s_in ? a.s_in + sbase : nullptr);
       else S.load_slot(e, slot_ptr(qu, u.wait_slot));
       float af[Carry<D>::NR], at[Carry<D>::NR];
@@ -323,6 +327,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
         for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
         combine_store<D>(e, S, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
         chain_publish(e, qu, u.pub_slot);
+        if (e.et == 0 && i == 0) KDA_TRACE_CTA(5, kda_globaltimer());
       }
       S.template write_operand<BF>(e, sb + L::SB, am);
       fence_async_smem();

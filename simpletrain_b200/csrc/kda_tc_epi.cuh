@@ -549,13 +549,24 @@ __device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int
 // stored thread-major like a slot.
 template <int D>
 __device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, const float (&A)[Carry<D>::NR],
-                                              const float4 *agg, float4 *dst) {
+                                              const float4 *__restrict__ agg, float4 *__restrict__ dst) {
+  // the loads of a batch are issued before its stores: a store between two loads
+  // would make each load a separate memory round trip (the pointers may alias
+  // as far as the compiler knows), which under a saturated memory system costs
+  // about a microsecond apiece
+  constexpr int N4 = Carry<D>::FLOATS / 4, BATCH = N4 < 4 ? N4 : 4;
   const float *f = &x.x[0][0];
-  for (int i4 = 0; i4 < Carry<D>::FLOATS / 4; ++i4) {
-    const float a = A[(4 * i4) / Carry<D>::NV];
-    const float4 g = __ldcg(agg + i4 * kEpi + e.et);
-    __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(a, f[4 * i4], g.x), fmaf(a, f[4 * i4 + 1], g.y),
-                                               fmaf(a, f[4 * i4 + 2], g.z), fmaf(a, f[4 * i4 + 3], g.w)));
+  for (int i0 = 0; i0 < N4; i0 += BATCH) {
+    float4 g[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) g[j] = __ldcg(agg + (i0 + j) * kEpi + e.et);
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int i4 = i0 + j;
+      const float a = A[(4 * i4) / Carry<D>::NV];
+      __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(a, f[4 * i4], g[j].x), fmaf(a, f[4 * i4 + 1], g[j].y),
+                                                 fmaf(a, f[4 * i4 + 2], g[j].z), fmaf(a, f[4 * i4 + 3], g[j].w)));
+    }
   }
 }
 
