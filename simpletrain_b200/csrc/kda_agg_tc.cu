@@ -1,21 +1,23 @@
 // Range aggregates for long streams (sm_100a, tcgen05 + TMEM + TMA).
 //
-// When (batch, head) streams are longer than a work range, a chain of ranges
-// hands the carry along each stream.  The carry recurrences are linear with a
-// diagonal (per key channel) decay, so the exit carry of a range's publishing
+// When (batch, head) streams are longer than a work range, the carry of a
+// stream passes through several ranges.  The carry recurrences are linear with
+// a diagonal (per key channel) decay, so the exit carry of a range's publishing
 // piece (a middle range, or the piece that starts -- reverse: ends -- a
-// stream, whose entry is the initial carry) is
+// stream) is
 //
 //   S_out = A S_in + S_loc,         A = decay^(64 n)   (n full chunks)
 //   T_out = A T_in + 64 n A S_in + T_loc               (decay tangent)
-//   dS_out = A dS_in + dS_loc                          (reverse pass)
+//   dS_out = A dS_in + dS_loc                          (reverse pass; a piece
+//                      that ends its stream holds the ragged last chunk)
 //
 // where the _loc terms are the same recurrences run from zero over the
-// piece's chunks.  This kernel computes them for every range (one CTA per
-// range, all in parallel), so the main kernels publish each exit carry as soon
-// as the entry carry is known instead of after the piece's full work, and no
-// range waits for a whole chain of earlier ones (kernels/kda_kernel.py:292-295
-// is the recurrence).
+// piece's chunks.
+// This kernel computes carry_loc for every range (one CTA per range, all in
+// parallel); each piece of the main kernels then folds its own entry carry
+// from the stream's boundary carry and the aggregates of the ranges before it
+// (fold_entry), so no range waits for another for its carry
+// (kernels/kda_kernel.py:292-295 is the recurrence).
 //
 //   MODE 0  S_loc from K, V            (forward)
 //   MODE 1  S_loc, T_loc from K, V     (backward, forward direction)
@@ -235,6 +237,52 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
   return cudaGetLastError();
 }
 
+// Entry carries of long streams, after the aggregates: for every range whose
+// first piece (reverse: last piece) continues a stream begun in another range,
+// the stream's boundary carry (initial state; reverse: final-state gradient;
+// `boundary`, or zero) folded through the aggregates of the ranges in between
+// (fold_entry) goes to the range's boundary slot, where the main kernel reads it
+// without waiting.  One CTA per range; the epilogue thread layout of the main
+// kernels, so the slot holds each thread's carry registers in their order.
+template <int D, bool REV, bool TAN>
+__global__ void __launch_bounds__(kThreads, 1) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
+  if (threadIdx.x < 64) return;
+  const Span sp = span_of(qu, (int)blockIdx.x, false);
+  Piece u;
+  u.range = sp.r;
+  if (!REV) {
+    if (sp.c0 == 0) return;  // starts its stream: nothing to fold
+    u.stream = sp.s0;
+  } else {
+    if (sp.c1 == qu.nchunks) return;
+    u.stream = sp.s1;
+  }
+  const Epi e;
+  Carry<D> x, t;
+  x.init_rows(e);
+  t.init_rows(e);
+  t.zero();
+  x.load_rm(e, boundary ? boundary + (size_t)u.stream * D * D : nullptr);
+  const int b = u.stream / a.H, h = u.stream - b * a.H;
+  const int Ltail = a.T - (qu.nchunks - 1) * 64;
+  float af[Carry<D>::NR], at[Carry<D>::NR];
+  for (int r = 0; r < Carry<D>::NR; ++r) {
+    af[r] = chunk_alpha(a.decay, b, h, x.row[r], 64, 64);
+    at[r] = chunk_alpha(a.decay, b, h, x.row[r], Ltail, 64);
+  }
+  fold_entry<D, REV, TAN>(e, qu, u, af, at, x, TAN ? &t : nullptr);
+  float4 *slot = slot_ptr(qu, REV ? sp.r + 1 : sp.r);
+  x.store_slot(e, slot);
+  if constexpr (TAN) t.store_slot(e, slot + (Carry<D>::FLOATS / 4) * kEpi);
+}
+
+template <int D, bool REV, bool TAN>
+cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary, cudaStream_t st) {
+  entry_fold_kernel<D, REV, TAN><<<q.nranges, kThreads, 0, st>>>(a, q, boundary);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 template <int MODE>
 cudaError_t agg_dispatch(const AggArgs &a, const View &va, const View &vb, const Queue &q, int dtype,
                          cudaStream_t st) {
@@ -262,10 +310,18 @@ cudaError_t agg_dispatch(const AggArgs &a, const View &va, const View &vb, const
 }  // namespace
 
 cudaError_t launch_agg_tc(int mode, const AggArgs &a, const View &va, const View &vb, const tc::Queue &q, int dtype,
-                          cudaStream_t st) {
-  if (mode == 0) return agg_dispatch<0>(a, va, vb, q, dtype, st);
-  if (mode == 1) return agg_dispatch<1>(a, va, vb, q, dtype, st);
-  return agg_dispatch<2>(a, va, vb, q, dtype, st);
+                          const float *boundary, cudaStream_t st) {
+  cudaError_t e = mode == 0 ? agg_dispatch<0>(a, va, vb, q, dtype, st)
+                  : mode == 1 ? agg_dispatch<1>(a, va, vb, q, dtype, st)
+                              : agg_dispatch<2>(a, va, vb, q, dtype, st);
+  if (e != cudaSuccess) return e;
+  if (a.D == 64)
+    return mode == 0 ? fold_launch<64, false, false>(a, q, boundary, st)
+           : mode == 1 ? fold_launch<64, false, true>(a, q, boundary, st)
+                       : fold_launch<64, true, false>(a, q, boundary, st);
+  return mode == 0 ? fold_launch<128, false, false>(a, q, boundary, st)
+         : mode == 1 ? fold_launch<128, false, true>(a, q, boundary, st)
+                     : fold_launch<128, true, false>(a, q, boundary, st);
 }
 
 }  // namespace kda

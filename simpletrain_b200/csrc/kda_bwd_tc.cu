@@ -339,7 +339,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       KDA_TAKE_UNIT(false)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      // entry state and tangent: the initial ones, or the ones at the range boundary
+      // (long streams: folded there before this kernel started; no wait)
+      const bool fold = u.folds(qu);
+      if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       if (e.et == 0 && i < 2) {
         KDA_TRACE_CTA(3 + 2 * i, kda_globaltimer());
         if (i == 0) KDA_TRACE_CTA(1, t);
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       constexpr int CF4 = Carry<D>::FLOATS / 4;  // float4 per thread of one carry
       // the previous range's decay-gradient share is added at the end of the piece
       for (int r = 0; r < Carry<D>::NR; ++r) dl[r] = 0.f;
-      if (prev) Td.load_slot(e, prev + CF4 * kEpi);
+      if (prev && !PS) Td.load_slot(e, prev + CF4 * kEpi);  // per-step mode carries no tangent
       else Td.zero();
       float af[Carry<D>::NR], at[Carry<D>::NR];
       const int Ltail = a.T - (qu.nchunks - 1) * 64;
@@ -366,49 +369,6 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         au_f = pow_log2(l2a, (float)(64 - kRef));
         for (int ee = 0; ee < 2; ++ee) rq[ee] = pow_log2(l2a, (float)(e.r0 + 8 * ee + 1 - kRef));
         rdo = pow_log2(l2a, (float)(make_do_row(e.et) + 1 - kRef));
-      }
-      const bool early = u.early(qu);
-      if (early) {
-        // exit state and tangent follow from the entry ones (the boundary slot, or at a
-        // stream start the initial state and a zero tangent) and the aggregate:
-        // S_out = A S_in + S_loc, T_out = A T_in + 64 n A S_in + T_loc
-        const float *sin = a.s_in ? a.s_in + sbase : nullptr;
-        const int n = u.c_end - u.c_begin;
-        float A[Carry<D>::NR], An[Carry<D>::NR];
-        for (int r = 0; r < Carry<D>::NR; ++r) {
-          A[r] = powf(af[r], (float)n);
-          An[r] = 64.f * (float)n * A[r];
-        }
-        const float4 *ag = agg_ptr(qu, u.range);
-        float4 *dst = slot_ptr(qu, u.pub_slot);
-        const float *ft = &Td.x[0][0];
-        // batches of float4 of S and of T; each batch's loads go out before its
-        // stores (a store between loads would make every load its own round trip)
-        constexpr int BATCH = CF4 < 2 ? CF4 : 2;
-        for (int i0 = 0; i0 < CF4; i0 += BATCH) {
-          float4 sv[BATCH], gs[BATCH], gt[BATCH];
-#pragma unroll
-          for (int j = 0; j < BATCH; ++j) {
-            const int i4 = i0 + j;
-            sv[j] = prev ? __ldcg(prev + i4 * kEpi + e.et)
-                         : sin ? Td.rm_f4(e, sin, i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            gs[j] = __ldcg(ag + i4 * kEpi + e.et);
-            if constexpr (!PS) gt[j] = __ldcg(ag + (CF4 + i4) * kEpi + e.et);  // no tangent in per-step mode
-          }
-#pragma unroll
-          for (int j = 0; j < BATCH; ++j) {
-            const int i4 = i0 + j, r = (4 * i4) / Carry<D>::NV;
-            __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(A[r], sv[j].x, gs[j].x), fmaf(A[r], sv[j].y, gs[j].y),
-                                                       fmaf(A[r], sv[j].z, gs[j].z), fmaf(A[r], sv[j].w, gs[j].w)));
-            if constexpr (!PS)
-              __stcg(dst + (CF4 + i4) * kEpi + e.et,
-                     make_float4(fmaf(A[r], ft[4 * i4], fmaf(An[r], sv[j].x, gt[j].x)),
-                                 fmaf(A[r], ft[4 * i4 + 1], fmaf(An[r], sv[j].y, gt[j].y)),
-                                 fmaf(A[r], ft[4 * i4 + 2], fmaf(An[r], sv[j].z, gt[j].z)),
-                                 fmaf(A[r], ft[4 * i4 + 3], fmaf(An[r], sv[j].w, gt[j].w))));
-          }
-        }
-        chain_publish(e, qu, u.pub_slot, 1);
       }
       bool ok = true;
       for (int c = u.c_begin; c < u.c_end; ++c, ++gc) {
@@ -613,7 +573,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       }
       if (u.pub_slot >= 0) {
         float4 *slot = slot_ptr(qu, u.pub_slot);
-        if (!early) {
+        if (!fold) {
           Carry<D> S;
           S.row[0] = Td.row[0];
           S.row[Carry<D>::NR - 1] = Td.row[Carry<D>::NR - 1];
@@ -843,7 +803,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       KDA_TAKE_UNIT(true)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      // dS at the piece's end: the final-state gradient, or the one at the range boundary
+      // (long streams: folded there before this kernel started; no wait)
+      const bool fold = u.folds(qu);
+      if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       if (u.wait_slot < 0) dS.load_rm(e, a.ds_out ? a.ds_out + sbase : nullptr);
       else dS.load_slot(e, slot_ptr(qu, u.wait_slot));
       float af[Carry<D>::NR], at[Carry<D>::NR];
@@ -862,17 +825,6 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         ad_f = pow_log2(l2a, (float)(64 - kRef));
         ad_0 = pow_log2(l2a, (float)(L0 - kRef));
         for (int ee = 0; ee < 2; ++ee) rk[ee] = pow_log2(l2a, (float)(kRef - 1 - e.r0 - 8 * ee));
-      }
-      const bool early = u.early(qu);
-      if (early) {
-        // dS at the piece's start follows from dS at its end and the aggregate; a piece
-        // that ends its stream includes the ragged last chunk (decay^Ltail)
-        const int n = u.c_end - u.c_begin;
-        const bool tail = u.c_end == qu.nchunks;
-        float A[Carry<D>::NR];
-        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
-        combine_store<D>(e, dS, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
-        chain_publish(e, qu, u.pub_slot);
       }
       dS.template write_operand<BF>(e, sb + L::SB, ad_0);
       fence_async_smem();
@@ -963,7 +915,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       }
       if (!ok) break;
       if (u.pub_slot >= 0) {
-        if (!early) {
+        if (!fold) {
           dS.store_slot(e, slot_ptr(qu, u.pub_slot));
           chain_publish(e, qu, u.pub_slot);
         }
@@ -1004,7 +956,7 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   const int dtype = BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16;
   if (q1.agg) {  // long streams: state (and tangent) aggregates from k, v
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q1.agg, q1.agg_f4, a.status};
-    if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, st)) != cudaSuccess) return e;
+    if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, a.s_in, st)) != cudaSuccess) return e;
   }
   k1<<<grid1, bwd_threads<PS>(), L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
   count_launches(1);
@@ -1012,7 +964,7 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
   if (e != cudaSuccess) return e;
   if (q2.agg) {  // long streams: dS aggregates from q and the dO the first pass wrote
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q2.agg, q2.agg_f4, a.status};
-    if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, st)) != cudaSuccess) return e;
+    if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, a.ds_out, st)) != cudaSuccess) return e;
   }
   k2<<<grid2, bwd_threads<PS>(), L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
   count_launches(1);

@@ -294,9 +294,11 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
       const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      // piece-start state: the initial state, or the one published at the range boundary
+      // piece-start state: the initial state, or the one at the range boundary
+      // (long streams: folded there before this kernel started; no wait)
+      const bool fold = u.folds(qu);
       if (e.et == 0) KDA_TRACE_EVENT(15, gc);
-      if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       if (e.et == 0) KDA_TRACE_EVENT(16, gc);
       if (e.et == 0 && i == 0) {
         KDA_TRACE_CTA(4, kda_globaltimer());
@@ -320,15 +322,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
         au_t = pow_log2(l2a, (float)(Ltail - kRef));
         for (int ee = 0; ee < 2; ++ee) rq[ee] = pow_log2(l2a, (float)(e.r0 + 8 * ee + 1 - kRef));
       }
-      const bool early = u.early(qu);
-      if (early) {
-        // the exit state follows from the entry state (slot or initial state) and the aggregate
-        float A[Carry<D>::NR];
-        for (int r = 0; r < Carry<D>::NR; ++r) A[r] = powf(af[r], (float)(u.c_end - u.c_begin));
-        combine_store<D>(e, S, A, agg_ptr(qu, u.range), slot_ptr(qu, u.pub_slot));
-        chain_publish(e, qu, u.pub_slot);
-        if (e.et == 0 && i == 0) KDA_TRACE_CTA(5, kda_globaltimer());
-      }
+      if (e.et == 0 && i == 0) KDA_TRACE_CTA(5, kda_globaltimer());
       S.template write_operand<BF>(e, sb + L::SB, am);
       fence_async_smem();
       named_bar_sync(1, kEpi);
@@ -397,7 +391,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
             KDA_TRACE_EVENT(9, gc);
           }
         } else if (u.pub_slot >= 0) {
-          if (!early) {
+          if (!fold) {
             // hand the state across the range boundary before storing the last y
             S.store_slot(e, slot_ptr(qu, u.pub_slot));
             chain_publish(e, qu, u.pub_slot);
@@ -497,9 +491,9 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
   auto kern = fwd_tc_kernel<T, D, LIT, PS, NS, NY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
-  if (q.agg) {  // long streams: the state aggregates first
+  if (q.agg) {  // long streams: the state aggregates and the range-boundary states first
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q.agg, q.agg_f4, a.status};
-    e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, st);
+    e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, a.s_in, st);
     if (e != cudaSuccess) return e;
   }
   kern<<<grid, fwd_threads<PS>(), L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);

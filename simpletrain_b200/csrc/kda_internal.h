@@ -90,7 +90,7 @@ cudaError_t launch_bwd_tc(const BwdArgs &a, const tc::Queue &q1, const tc::Queue
 // mode 0: S from (k, v); 1: S and decay tangent from (k, v); 2: dS from (q, dO).
 // a.per_step takes modes 0 and 2.
 cudaError_t launch_agg_tc(int mode, const AggArgs &a, const View &va, const View &vb, const tc::Queue &q, int dtype,
-                          cudaStream_t st);
+                          const float *boundary, cudaStream_t st);
 // CTAs of the forward kernel that fit on one SM.
 int fwd_tc_occupancy(int D, int dtype, bool literal, bool per_step);
 

@@ -153,18 +153,6 @@ struct Carry {
         }
     }
   }
-  // float4 number i4 of this thread's registers (the slot order), read straight
-  // from a row-major [D][D] state instead of being held in registers
-  __device__ float4 rm_f4(const Epi &e, const float *src, int i4) const {
-    const int r = (4 * i4) / NV, i = (4 * i4) % NV;
-    if constexpr (D == 128) {
-      return __ldg(reinterpret_cast<const float4 *>(src + (size_t)row[0] * D + W * e.cg + i));
-    } else {
-      const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + (size_t)row[r] * D + col(e, i)));
-      const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + (size_t)row[r] * D + col(e, i + 2)));
-      return make_float4(lo.x, lo.y, hi.x, hi.y);
-    }
-  }
   __device__ void store_rm(const Epi &e, float *dst) const {
     if constexpr (D == 128) {
       float4 *d4 = reinterpret_cast<float4 *>(dst + (size_t)row[0] * D + W * e.cg);
@@ -432,10 +420,10 @@ struct Piece {
   int wait_slot;               // boundary slot holding the entry state, or -1 (stream end / start)
   int pub_slot;                // boundary slot for the exit state, or -1
   int range;
-  // with precomputed aggregates (long streams), a piece that publishes does so
-  // as soon as its entry state is known: from the boundary slot, or at the
-  // start of its stream the initial state
-  __device__ __forceinline__ bool early(const Queue &qu) const { return pub_slot >= 0 && qu.agg != nullptr; }
+  // with precomputed aggregates (long streams) the entry carries of all range
+  // boundaries are folded from them before the main kernel starts (fold_entry),
+  // so a piece reads its entry without waiting and publishes no exit carry
+  __device__ __forceinline__ bool folds(const Queue &qu) const { return qu.agg != nullptr; }
 };
 
 // Range of ticket t: stream-major positions [N t / R, N (t+1) / R), N = streams x chunks.
@@ -494,6 +482,15 @@ __device__ __forceinline__ bool published_piece(const Queue &qu, const Span &sp,
   return true;
 }
 
+// Range whose work holds global chunk x = stream * nchunks + chunk.
+__device__ __forceinline__ int range_of(const Queue &qu, long long x) {
+  const long long n = (long long)qu.nstreams * qu.nchunks;
+  int r = (int)(x * qu.nranges / n);
+  while (r + 1 < qu.nranges && n * (r + 1) / qu.nranges <= x) ++r;
+  while (r > 0 && n * r / qu.nranges > x) --r;
+  return r;
+}
+
 __device__ __forceinline__ float4 *slot_ptr(const Queue &qu, int slot) {
   return qu.slots + (size_t)slot * qu.slot_f4 * kEpi;
 }
@@ -544,28 +541,56 @@ __device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int
   }
 }
 
-// Exit carry of a publishing piece from its entry carry x and its aggregate:
-// out = A x + agg (A = the product of the piece's chunk decays per row),
-// stored thread-major like a slot.
-template <int D>
-__device__ __forceinline__ void combine_store(const Epi &e, const Carry<D> &x, const float (&A)[Carry<D>::NR],
-                                              const float4 *__restrict__ agg, float4 *__restrict__ dst) {
-  // the loads of a batch are issued before its stores: a store between two loads
-  // would make each load a separate memory round trip (the pointers may alias
-  // as far as the compiler knows), which under a saturated memory system costs
-  // about a microsecond apiece
-  constexpr int N4 = Carry<D>::FLOATS / 4, BATCH = N4 < 4 ? N4 : 4;
-  const float *f = &x.x[0][0];
-  for (int i0 = 0; i0 < N4; i0 += BATCH) {
-    float4 g[BATCH];
+// Entry carry of piece u on a long stream, without waiting for another range:
+// x holds the stream's boundary carry (forward: the initial state; reverse: the
+// final-state gradient) and is folded through the aggregates of the publishing
+// pieces of the ranges between that boundary and u, in stream order:
+//   x <- A_j x + x_loc_j,  and with a tangent (TAN)  t <- A_j t + 64 n_j A_j x + t_loc_j,
+// A_j the product of piece j's chunk decays (decay^(64 n_j); reverse, at the
+// stream's end, decay^(64 (n_j - 1) + L_tail)).  The same recurrence the chain of
+// boundary slots would carry, evaluated by every piece for itself.
+template <int D, bool REV, bool TAN>
+__device__ void fold_entry(const Epi &e, const Queue &qu, const Piece &u, const float (&af)[Carry<D>::NR],
+                           const float (&at)[Carry<D>::NR], Carry<D> &x, Carry<D> *t) {
+  constexpr int NR = Carry<D>::NR, N4 = Carry<D>::FLOATS / 4, BATCH = TAN ? 4 : (N4 < 8 ? N4 : 8);
+  const long long edge = (long long)u.stream * qu.nchunks + (REV ? qu.nchunks - 1 : 0);
+  float *f = &x.x[0][0];
+  for (int j = range_of(qu, edge); j != u.range; j += REV ? -1 : 1) {
+    int s, cb, ce;
+    published_piece(qu, span_of(qu, j, false), REV, s, cb, ce);
+    const int n = ce - cb;
+    const bool tail = REV && ce == qu.nchunks;
+    float A[NR], An[NR];
+    for (int r = 0; r < NR; ++r) {
+      A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
+      An[r] = 64.f * (float)n * A[r];
+    }
+    const float4 *ag = agg_ptr(qu, j);
+    for (int i0 = 0; i0 < N4; i0 += BATCH) {
+      float4 g[BATCH], gt[BATCH];
 #pragma unroll
-    for (int j = 0; j < BATCH; ++j) g[j] = __ldcg(agg + (i0 + j) * kEpi + e.et);
+      for (int k = 0; k < BATCH; ++k) {
+        g[k] = __ldcg(ag + (i0 + k) * kEpi + e.et);
+        if constexpr (TAN) gt[k] = __ldcg(ag + (N4 + i0 + k) * kEpi + e.et);
+      }
 #pragma unroll
-    for (int j = 0; j < BATCH; ++j) {
-      const int i4 = i0 + j;
-      const float a = A[(4 * i4) / Carry<D>::NV];
-      __stcg(dst + i4 * kEpi + e.et, make_float4(fmaf(a, f[4 * i4], g[j].x), fmaf(a, f[4 * i4 + 1], g[j].y),
-                                                 fmaf(a, f[4 * i4 + 2], g[j].z), fmaf(a, f[4 * i4 + 3], g[j].w)));
+      for (int k = 0; k < BATCH; ++k) {
+        const int i4 = i0 + k, r = (4 * i4) / Carry<D>::NV;
+        const float gv[4] = {g[k].x, g[k].y, g[k].z, g[k].w};
+        float tv[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (TAN) {
+          tv[0] = gt[k].x; tv[1] = gt[k].y; tv[2] = gt[k].z; tv[3] = gt[k].w;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float &xv = f[4 * i4 + c];
+          if constexpr (TAN) {
+            float &tx = (&t->x[0][0])[4 * i4 + c];
+            tx = fmaf(A[r], tx, fmaf(An[r], xv, tv[c]));
+          }
+          xv = fmaf(A[r], xv, gv[c]);
+        }
+      }
     }
   }
 }
