@@ -16,7 +16,7 @@
 // This kernel computes carry_loc for every range (one CTA per range, all in
 // parallel); each piece of the main kernels then folds its own entry carry
 // from the stream's boundary carry and the aggregates of the ranges before it
-// (fold_entry), so no range waits for another for its carry
+// (entry_fold_kernel), so no range waits for another for its carry
 // (kernels/kda_kernel.py:292-295 is the recurrence).
 //
 //   MODE 0  S_loc from K, V            (forward)
@@ -239,46 +239,96 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
 
 // Entry carries of long streams, after the aggregates: for every range whose
 // first piece (reverse: last piece) continues a stream begun in another range,
-// the stream's boundary carry (initial state; reverse: final-state gradient;
-// `boundary`, or zero) folded through the aggregates of the ranges in between
-// (fold_entry) goes to the range's boundary slot, where the main kernel reads it
-// without waiting.  One CTA per range; the epilogue thread layout of the main
-// kernels, so the slot holds each thread's carry registers in their order.
+// the stream's boundary carry x (initial state; reverse: final-state gradient;
+// `boundary`, or zero) is folded through the aggregates of the publishing pieces
+// of the ranges in between, in stream order,
+//   x <- A_j x + x_loc_j    (with the tangent: t <- A_j t + 64 n_j A_j x + t_loc_j),
+// A_j the product of piece j's chunk decays, and goes to the range's boundary
+// slot, where the main kernel reads it without waiting.  The epilogue thread
+// layout of the main kernels (slot = each thread's carry registers in order);
+// grid (ranges, kFoldParts): each CTA folds one slice of every thread's carry,
+// so a thread holds its slice of an aggregate in one batch of loads and pays
+// one memory round trip per range it folds.
+constexpr int kFoldParts = 4;
+
 template <int D, bool REV, bool TAN>
-__global__ void __launch_bounds__(kThreads, 1) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
+__global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
   if (threadIdx.x < 64) return;
   const Span sp = span_of(qu, (int)blockIdx.x, false);
-  Piece u;
-  u.range = sp.r;
+  int stream;
   if (!REV) {
     if (sp.c0 == 0) return;  // starts its stream: nothing to fold
-    u.stream = sp.s0;
+    stream = sp.s0;
   } else {
     if (sp.c1 == qu.nchunks) return;
-    u.stream = sp.s1;
+    stream = sp.s1;
   }
+  constexpr int NR = Carry<D>::NR, NV = Carry<D>::NV, N4 = Carry<D>::FLOATS / 4, NP = N4 / kFoldParts;
+  static_assert(N4 % kFoldParts == 0, "carry slices");
   const Epi e;
-  Carry<D> x, t;
-  x.init_rows(e);
-  t.init_rows(e);
-  t.zero();
-  x.load_rm(e, boundary ? boundary + (size_t)u.stream * D * D : nullptr);
-  const int b = u.stream / a.H, h = u.stream - b * a.H;
-  const int Ltail = a.T - (qu.nchunks - 1) * 64;
-  float af[Carry<D>::NR], at[Carry<D>::NR];
-  for (int r = 0; r < Carry<D>::NR; ++r) {
-    af[r] = chunk_alpha(a.decay, b, h, x.row[r], 64, 64);
-    at[r] = chunk_alpha(a.decay, b, h, x.row[r], Ltail, 64);
+  Carry<D> rows;  // row and column indices of this thread's carry registers only
+  rows.init_rows(e);
+  const int i0 = (int)blockIdx.y * NP;
+  // boundary carry, float4 i4 of this thread's registers = row-major columns col(i)..col(i)+3
+  float4 xs[NP], ts[NP];
+  for (int k = 0; k < NP; ++k) {
+    const int i4 = i0 + k, r = (4 * i4) / NV, c = (4 * i4) % NV;
+    xs[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    ts[k] = xs[k];
+    if (boundary) {
+      const float *src = boundary + (size_t)stream * D * D + (size_t)rows.row[r] * D;
+      const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + rows.col(e, c)));
+      const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + rows.col(e, c + 2)));
+      xs[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
   }
-  fold_entry<D, REV, TAN>(e, qu, u, af, at, x, TAN ? &t : nullptr);
+  const int b = stream / a.H, h = stream - b * a.H;
+  const int Ltail = a.T - (qu.nchunks - 1) * 64;
+  float af[NR], at[NR];
+  for (int r = 0; r < NR; ++r) {
+    af[r] = chunk_alpha(a.decay, b, h, rows.row[r], 64, 64);
+    at[r] = chunk_alpha(a.decay, b, h, rows.row[r], Ltail, 64);
+  }
+  const long long edge = (long long)stream * qu.nchunks + (REV ? qu.nchunks - 1 : 0);
+  for (int j = range_of(qu, edge); j != sp.r; j += REV ? -1 : 1) {
+    int s, cb, ce;
+    published_piece(qu, span_of(qu, j, false), REV, s, cb, ce);
+    const int n = ce - cb;
+    const bool tail = REV && ce == qu.nchunks;
+    const float4 *ag = agg_ptr(qu, j);
+    float4 g[NP], gt[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+      g[k] = __ldcg(ag + (i0 + k) * kEpi + e.et);
+      if constexpr (TAN) gt[k] = __ldcg(ag + (N4 + i0 + k) * kEpi + e.et);
+    }
+    float A[NR], An[NR];
+    for (int r = 0; r < NR; ++r) {
+      A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
+      An[r] = 64.f * (float)n * A[r];
+    }
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+      const int r = (4 * (i0 + k)) / NV;
+      if constexpr (TAN)
+        ts[k] = make_float4(fmaf(A[r], ts[k].x, fmaf(An[r], xs[k].x, gt[k].x)),
+                            fmaf(A[r], ts[k].y, fmaf(An[r], xs[k].y, gt[k].y)),
+                            fmaf(A[r], ts[k].z, fmaf(An[r], xs[k].z, gt[k].z)),
+                            fmaf(A[r], ts[k].w, fmaf(An[r], xs[k].w, gt[k].w)));
+      xs[k] = make_float4(fmaf(A[r], xs[k].x, g[k].x), fmaf(A[r], xs[k].y, g[k].y), fmaf(A[r], xs[k].z, g[k].z),
+                          fmaf(A[r], xs[k].w, g[k].w));
+    }
+  }
   float4 *slot = slot_ptr(qu, REV ? sp.r + 1 : sp.r);
-  x.store_slot(e, slot);
-  if constexpr (TAN) t.store_slot(e, slot + (Carry<D>::FLOATS / 4) * kEpi);
+  for (int k = 0; k < NP; ++k) {
+    __stcg(slot + (i0 + k) * kEpi + e.et, xs[k]);
+    if constexpr (TAN) __stcg(slot + (N4 + i0 + k) * kEpi + e.et, ts[k]);
+  }
 }
 
 template <int D, bool REV, bool TAN>
 cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary, cudaStream_t st) {
-  entry_fold_kernel<D, REV, TAN><<<q.nranges, kThreads, 0, st>>>(a, q, boundary);
+  entry_fold_kernel<D, REV, TAN><<<dim3(q.nranges, kFoldParts), kThreads, 0, st>>>(a, q, boundary);
   count_launches(1);
   return cudaGetLastError();
 }

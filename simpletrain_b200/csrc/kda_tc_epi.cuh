@@ -421,8 +421,9 @@ struct Piece {
   int pub_slot;                // boundary slot for the exit state, or -1
   int range;
   // with precomputed aggregates (long streams) the entry carries of all range
-  // boundaries are folded from them before the main kernel starts (fold_entry),
-  // so a piece reads its entry without waiting and publishes no exit carry
+  // boundaries are folded from them before the main kernel starts
+  // (entry_fold_kernel), so a piece reads its entry without waiting and
+  // publishes no exit carry
   __device__ __forceinline__ bool folds(const Queue &qu) const { return qu.agg != nullptr; }
 };
 
@@ -538,60 +539,6 @@ __device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int
   if (e.et == 0) {
     __threadfence();
     atomicExch(qu.flags + slot, level);
-  }
-}
-
-// Entry carry of piece u on a long stream, without waiting for another range:
-// x holds the stream's boundary carry (forward: the initial state; reverse: the
-// final-state gradient) and is folded through the aggregates of the publishing
-// pieces of the ranges between that boundary and u, in stream order:
-//   x <- A_j x + x_loc_j,  and with a tangent (TAN)  t <- A_j t + 64 n_j A_j x + t_loc_j,
-// A_j the product of piece j's chunk decays (decay^(64 n_j); reverse, at the
-// stream's end, decay^(64 (n_j - 1) + L_tail)).  The same recurrence the chain of
-// boundary slots would carry, evaluated by every piece for itself.
-template <int D, bool REV, bool TAN>
-__device__ void fold_entry(const Epi &e, const Queue &qu, const Piece &u, const float (&af)[Carry<D>::NR],
-                           const float (&at)[Carry<D>::NR], Carry<D> &x, Carry<D> *t) {
-  constexpr int NR = Carry<D>::NR, N4 = Carry<D>::FLOATS / 4, BATCH = TAN ? 4 : (N4 < 8 ? N4 : 8);
-  const long long edge = (long long)u.stream * qu.nchunks + (REV ? qu.nchunks - 1 : 0);
-  float *f = &x.x[0][0];
-  for (int j = range_of(qu, edge); j != u.range; j += REV ? -1 : 1) {
-    int s, cb, ce;
-    published_piece(qu, span_of(qu, j, false), REV, s, cb, ce);
-    const int n = ce - cb;
-    const bool tail = REV && ce == qu.nchunks;
-    float A[NR], An[NR];
-    for (int r = 0; r < NR; ++r) {
-      A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
-      An[r] = 64.f * (float)n * A[r];
-    }
-    const float4 *ag = agg_ptr(qu, j);
-    for (int i0 = 0; i0 < N4; i0 += BATCH) {
-      float4 g[BATCH], gt[BATCH];
-#pragma unroll
-      for (int k = 0; k < BATCH; ++k) {
-        g[k] = __ldcg(ag + (i0 + k) * kEpi + e.et);
-        if constexpr (TAN) gt[k] = __ldcg(ag + (N4 + i0 + k) * kEpi + e.et);
-      }
-#pragma unroll
-      for (int k = 0; k < BATCH; ++k) {
-        const int i4 = i0 + k, r = (4 * i4) / Carry<D>::NV;
-        const float gv[4] = {g[k].x, g[k].y, g[k].z, g[k].w};
-        float tv[4] = {0.f, 0.f, 0.f, 0.f};
-        if constexpr (TAN) {
-          tv[0] = gt[k].x; tv[1] = gt[k].y; tv[2] = gt[k].z; tv[3] = gt[k].w;
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float &xv = f[4 * i4 + c];
-          if constexpr (TAN) {
-            float &tx = (&t->x[0][0])[4 * i4 + c];
-            tx = fmaf(A[r], tx, fmaf(An[r], xv, tv[c]));
-          }
-          xv = fmaf(A[r], xv, gv[c]);
-        }
-      }
-    }
   }
 }
 
