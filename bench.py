@@ -285,7 +285,9 @@ def run_e2e(args, w, rank, world, dev, inp):
     copies its inputs (q, k, v, g, dy, decay, initial state) from pinned host
     memory to the device and its results (y, final state, dq, dk, dv, dg,
     d_decay, d_initial_state) back, inside the timed region; the batch is
-    pipelined in slices so both copy directions overlap the kernels."""
+    pipelined in slices so both copy directions overlap the kernels, and each
+    step is submitted before the previous step's results are awaited, so one
+    step's copies in overlap the previous step's copies out."""
     import torch.distributed as dist
 
     from simpletrain_b200.host_stream import HostScan
@@ -307,23 +309,29 @@ def run_e2e(args, w, rank, world, dev, inp):
     h2d += decay.numel() * decay.element_size()
     d2h = 0
 
-    def one():
+    def run(n):
+        """n steps, each submitted before the previous one's results are awaited."""
         nonlocal d2h
-        out = scan(host["q"], host["k"], host["v"], host["g"], decay, dy=host.get("dy"),
-                   initial_state=host.get("s0"))
-        d2h = sum(o.numel() * o.element_size() for o in out.values())
+        pend = None
+        for i in range(n + 1):
+            nxt = None
+            if i < n:
+                nxt = scan.submit(host["q"], host["k"], host["v"], host["g"], decay, dy=host.get("dy"),
+                                  initial_state=host.get("s0"))
+            if pend is not None:
+                out = pend.wait()
+                d2h = sum(o.numel() * o.element_size() for o in out.values())
+            pend = nxt
 
-    for _ in range(2):
-        one()
+    run(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     stream = torch.cuda.current_stream(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(steps):
-        one()
-    b.record(stream)
+    run(steps)
+    b.record(stream)     # after the last step's results were awaited on the host
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -333,8 +341,9 @@ def run_e2e(args, w, rank, world, dev, inp):
     return {"value": round(world * w.B * w.T * steps / (ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "slices": scan.slices if scan.slices is not None else min(w.B, 16),
-            "api": "simpletrain_b200.host_stream.HostScan (pinned host buffers, batch slices pipelined "
-                   "over copy-in / scan / copy-out streams)"}
+            "api": "simpletrain_b200.host_stream.HostScan.submit + wait (pinned host buffers, batch slices "
+                   "pipelined over copy-in / scan / copy-out streams, each step submitted before the "
+                   "previous step's results are awaited)"}
 
 
 # --------------------------------------------------------------------------- #
@@ -549,7 +558,7 @@ def main():
     ap.add_argument("--fwd-only", action="store_true", help="with --shape: forward pass only")
     ap.add_argument("--per-step", action="store_true",
                     help="per-token decay semantics (one decay per head) instead of chunk-constant decay")
-    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-slices", type=int, default=None,
                     help="batch slices of the host-buffer pipeline (default min(B, 16))")

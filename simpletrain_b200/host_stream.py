@@ -17,8 +17,14 @@ batch is summed over all rows on the device before it is copied back.
 Host tensors should be pinned (``pin_memory=True``): copies from pageable
 memory are staged by the driver and overlap nothing.  Device buffers and the
 pinned result buffers are kept for the next call with the same shapes; the
-returned tensors are those buffers, valid until the next call (clone them to
-keep them).  One call at a time per object.
+returned tensors are those buffers.  ``scan(...)`` returns when its results
+are on the host, valid until the second call after it (clone them to keep
+them).  ``scan.submit(...)`` returns at once with a ``Pending`` whose
+``wait()`` gives the results: two submitted calls overlap (the next call's
+copies in run while this one's results come back), with two sets of result
+buffers used in turn, so a call's results stay valid until the second
+submission after it, which first waits for it.  A submitted call's host
+inputs must stay unchanged until its ``wait()`` returns.
 """
 from __future__ import annotations
 
@@ -29,13 +35,25 @@ from torch import Tensor
 
 from .ops import MODE_CORRECTED, MODE_LITERAL, MODE_PER_STEP, decay_as_bhd, per_step_decay
 
-__all__ = ["HostScan"]
+__all__ = ["HostScan", "Pending"]
 
 _DTYPES = (torch.bfloat16, torch.float16)
 
 
 def _pinned_like(t: Tensor) -> Tensor:
     return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device="cpu", pin_memory=True)
+
+
+class Pending:
+    """A submitted ``HostScan`` call: ``wait()`` blocks until its results are on the host."""
+
+    def __init__(self, results: Dict[str, Tensor], finished: torch.cuda.Event):
+        self._results = results
+        self._finished = finished
+
+    def wait(self) -> Dict[str, Tensor]:
+        self._finished.synchronize()
+        return self._results
 
 
 class HostScan:
@@ -68,25 +86,42 @@ class HostScan:
         self.per_step = per_step
         self._key = None
         self._streams = None
+        self._pending = [None, None]   # the last call on each result-buffer set
+        self._turn = 0                 # result-buffer set of the next call
+        self._slice_done = []          # per slice: the last call's scan of it (reads the device inputs)
 
     # ------------------------------------------------------------------ #
     def _buffers(self, key, tensors: Dict[str, Tensor], outs: Dict[str, tuple]):
-        """(Re)allocate device inputs and pinned host results for a new shape."""
+        """(Re)allocate device inputs and two sets of pinned host results for a new shape."""
         if key == self._key:
             return
+        for p in self._pending:   # calls in flight still use the old buffers
+            if p is not None:
+                p.wait()
+        self._pending = [None, None]
+        self._slice_done = []
         self.dev_in = {n: torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=self.device)
                        for n, t in tensors.items()}
-        self.host_out = {}
-        for n, (like, shape) in outs.items():
-            if like is not None:
-                self.host_out[n] = _pinned_like(like)
-            else:
-                self.host_out[n] = torch.empty(shape, dtype=torch.float32, pin_memory=True)
+        self.host_out = []
+        for _ in range(2):
+            ho = {}
+            for n, (like, shape) in outs.items():
+                if like is not None:
+                    ho[n] = _pinned_like(like)
+                else:
+                    ho[n] = torch.empty(shape, dtype=torch.float32, pin_memory=True)
+            self.host_out.append(ho)
         self._key = key
 
     def __call__(self, q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
                  decay: Union[float, Tensor] = 0.99, dy: Optional[Tensor] = None,
                  initial_state: Optional[Tensor] = None, output_final_state: bool = True) -> Dict[str, Tensor]:
+        return self.submit(q, k, v, g, decay, dy, initial_state, output_final_state).wait()
+
+    def submit(self, q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor] = None,
+               decay: Union[float, Tensor] = 0.99, dy: Optional[Tensor] = None,
+               initial_state: Optional[Tensor] = None, output_final_state: bool = True) -> Pending:
+        """Queue the call and return at once; ``wait()`` on the result gives what ``__call__`` returns."""
         if q.dim() != 4:
             raise ValueError(f"q must be [B, H, T, D], got shape {tuple(q.shape)}")
         if q.dtype not in _DTYPES:
@@ -149,14 +184,22 @@ class HostScan:
             dd_rows = torch.empty((B, H, D), dtype=torch.float32, device=dev) if want_dd else None
         s_in.wait_stream(caller)
 
+        # this call's result buffers: the set of the call before the last, once that has finished
+        turn = self._turn
+        self._turn ^= 1
+        if self._pending[turn] is not None:
+            self._pending[turn].wait()
         n_sl = max(1, min(B, self.slices if self.slices is not None else 16))
         bounds = [(B * i // n_sl, B * (i + 1) // n_sl) for i in range(n_sl)]
-        di, ho = self.dev_in, self.host_out
-        for b0, b1 in bounds:
+        di, ho = self.dev_in, self.host_out[turn]
+        prev_done, slice_done = self._slice_done, []
+        for i, (b0, b1) in enumerate(bounds):
             if b1 == b0:
                 continue
-            # copy in
+            # copy in, once the last call's scan of this slice has read the device inputs
             with torch.cuda.stream(s_in):
+                if i < len(prev_done) and prev_done[i] is not None:
+                    s_in.wait_event(prev_done[i])
                 for n, t in named.items():
                     di[n][b0:b1].copy_(t[b0:b1], non_blocking=True)
                 arrived = torch.cuda.Event()
@@ -185,6 +228,9 @@ class HostScan:
                         res["ds0"] = gs0
                 done = torch.cuda.Event()
                 done.record(s_run)
+            while len(slice_done) < i:
+                slice_done.append(None)
+            slice_done.append(done)
             # copy out
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done)
@@ -202,7 +248,9 @@ class HostScan:
                 s_out.wait_event(done)
                 red.record_stream(s_out)
                 ho["ddecay"].copy_(red, non_blocking=True)
-        for s in (s_in, s_run, s_out):
-            caller.wait_stream(s)
-        caller.synchronize()
-        return dict(ho)
+        self._slice_done = slice_done
+        finished = torch.cuda.Event()
+        finished.record(s_out)
+        pending = Pending(dict(ho), finished)
+        self._pending[turn] = pending
+        return pending

@@ -105,11 +105,28 @@ def test_host_scan_reuses_buffers_and_new_shapes():
     a = scan(q, k, v, g, 0.9, dy=dy)
     ptr = a["y"].data_ptr()
     ref = {n: t.clone() for n, t in a.items()}
-    b = scan(q, k, v, g, 0.9, dy=dy)
-    assert b["y"].data_ptr() == ptr
+    b = scan(q, k, v, g, 0.9, dy=dy)        # the second result-buffer set
+    c = scan(q, k, v, g, 0.9, dy=dy)        # the first one again
+    assert b["y"].data_ptr() != ptr and c["y"].data_ptr() == ptr
     for n in ref:
-        assert torch.equal(b[n], ref[n]), n   # same inputs, same slices: identical
+        assert torch.equal(b[n], ref[n]) and torch.equal(c[n], ref[n]), n   # same inputs and slices: identical
     b["dq"].add_(1)   # ordinary tensors: in-place use outside inference mode works
     q2, k2, v2, g2, dy2, _ = _inputs(3, 2, 64, 64, seed=25)
     c = scan(q2, k2, v2, g2, 0.9, dy=dy2)
     _check(c, _device_reference(q2, k2, v2, g2, 0.9, dy2, None))
+
+
+def test_host_scan_submitted_calls_overlap_and_keep_their_results():
+    """Calls queued with submit() before waiting: each gets its own inputs' results."""
+    scan = HostScan(DEV, slices=4)
+    batches = [_inputs(4, 2, 192, 128, seed=30 + i) for i in range(4)]
+    decay = torch.sigmoid(torch.randn(2, 128, generator=torch.Generator().manual_seed(3)) + 3.0)
+    pend, got = None, []
+    for q, k, v, g, dy, _ in batches:
+        p = scan.submit(q, k, v, g, decay, dy=dy)
+        if pend is not None:
+            got.append({n: t.clone() for n, t in pend.wait().items()})
+        pend = p
+    got.append({n: t.clone() for n, t in pend.wait().items()})
+    for (q, k, v, g, dy, _), res in zip(batches, got):
+        _check(res, _device_reference(q, k, v, g, decay, dy, None))
