@@ -163,8 +163,10 @@ uint64_t kda_launch_count(void);
      needs more than KDA_NOALLOC_SCRATCH_BYTES of scratch
      (kda_fwd_workspace_bytes() tells how much: 64 KiB per range boundary at
      D=128, 16 KiB at D=64, at most one boundary per resident CTA -- about
-     10 MiB on a 148-SM GPU -- plus a small header; only a KDA_SM100_RANGES
-     override far above the CTA count reaches the limit).
+     10 MiB on a 148-SM GPU -- and, when a stream spans three or more ranges,
+     one range aggregate of the same size per range -- about 19 MiB in all --
+     plus a small header; only a KDA_SM100_RANGES override far above the CTA
+     count reaches the limit).
    - The first call on a device looks up the array's device address; make that
      first call before any stream capture.
    - Calls share the array and it keeps the last call's contents; each call

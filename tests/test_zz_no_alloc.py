@@ -59,7 +59,10 @@ def _noalloc(q, k, v, g, decay_bhd, s0):
     return y, s_out
 
 
-@pytest.mark.parametrize("B,H,T,D", [(4, 6, 600, 128), (16, 10, 512, 128), (3, 5, 1000, 64)])
+@pytest.mark.parametrize("B,H,T,D", [
+    (4, 6, 600, 128), (16, 10, 512, 128), (3, 5, 1000, 64),
+    (1, 2, 4096, 128),   # long streams: range aggregates and folded entries in the scratch too
+])
 def test_noalloc_matches_allocating_entry_point_twice(B, H, T, D):
     w = custom(B, H, T, D, backward=False, s0_std=0.02)
     inp = make_inputs(w, seed=3, device="cuda")
