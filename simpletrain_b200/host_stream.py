@@ -61,11 +61,12 @@ class HostScan:
 
     ``HostScan(device=None, slices=None, chunk_size=64, per_step=False,
     reference_exact=False)``; ``slices`` defaults to ``min(B, 16)`` batch
-    slices (on the 1b shape, B=16, fwd+bwd: 4 slices 2.68 M, 8 slices 2.84 M,
-    16 slices 2.96 M tokens/s).  Calling it with q, k, v (``[B, H, T, D]``
-    bf16/fp16 host tensors, any strides with the batch dimension outermost in
-    memory, such as the
-    ``[B, T, H, D]``-memory views the KDA layer produces), an optional gate,
+    slices (on the 1b shape, B=16, fwd+bwd, one call at a time: 4 slices
+    2.68 M, 8 slices 2.84 M, 16 slices 2.96 M tokens/s; with ``submit``
+    overlapping consecutive calls, 3.1-3.3 M).  Calling it with q, k, v
+    (``[B, H, T, D]`` bf16/fp16 host tensors, any strides with the batch
+    dimension outermost in memory, such as the ``[B, T, H, D]``-memory views
+    the KDA layer produces), an optional gate,
     the decay (float or tensor, as for ``kda_chunk``), an optional ``dy`` and
     initial state returns a dict of host tensors: ``y`` and ``final_state``;
     with ``dy`` also ``dq``, ``dk``, ``dv``, ``dg`` (with a gate), ``ddecay``
