@@ -395,3 +395,33 @@ def per_step_manual_backward(q, k, v, gate, decay, chunk_size: int,
         dv[:, :, t0:t1] = P.transpose(-1, -2) @ dOh + Kt @ dSh
         dS = a4 ** L * dS + a4 ** m * (Qc.transpose(-1, -2) @ dOh)
     return dq, dk, dv, dg, dS
+
+
+# --------------------------------------------------------------------------- #
+# the layer around the scan
+# --------------------------------------------------------------------------- #
+def layer_forward(params: dict, x: torch.Tensor, n_heads: int, d_head: int,
+                  chunk_size: int, mode: str) -> torch.Tensor:
+    """SimpleTrain's ``KimiDeltaAttention.forward`` (``models/kimi_k3.py:94-125``)
+    in fp32 over ``chunk_scan``: [B, T, d_model] -> [B, T, d_model].
+
+    ``params`` holds the layer's tensors by its parameter names (``q_proj.weight``
+    ... ``o_proj.weight``, ``log_decay``).  Steps: four bias-free projections
+    viewed as [B, H, T, Dh] (``:99-102``); the scan with the detached mean of
+    ``exp(log_decay).clamp(1e-3, 0.999)`` as a float decay (``:105-118``); the
+    per-head scale by the same clamped exponential, not detached (``:121-122``);
+    the transpose back and ``o_proj`` (``:124-125``).  Differentiable by autograd.
+    """
+    B, T, _ = x.shape
+    H, Dh = n_heads, d_head
+
+    def proj(name):
+        return torch.matmul(x, params[f"{name}.weight"].t()).view(B, T, H, Dh).transpose(1, 2)
+
+    q, k, v, g = (proj(n) for n in ("q_proj", "k_proj", "v_proj", "g_proj"))
+    decay = float(torch.exp(params["log_decay"]).clamp(min=1e-3, max=0.999).detach().mean())
+    o, _ = chunk_scan(q, k, v, g, decay, chunk_size, mode=mode)
+    head_scale = torch.exp(params["log_decay"]).clamp(min=1e-3, max=0.999)
+    o = o * head_scale.view(1, H, 1, 1)
+    o = o.transpose(1, 2).contiguous().view(B, T, H * Dh)
+    return torch.matmul(o, params["o_proj.weight"].t())

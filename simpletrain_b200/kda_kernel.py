@@ -9,11 +9,20 @@ Same public names and argument meaning as the reference module:
 * ``_supported_arch()``                        (``kernels/kda_kernel.py:58-67``)
 
 Both scan functions run the sm_100a kernels through the ``kda_b200`` custom
-op; ``use_triton`` is accepted and ignored (there is one implementation and no
-fallback).  The result keeps the reference's conventions: y has q's dtype,
-shape and memory order (``:263``), the state is not returned (``:297``), and
-``decay`` is a float or a tensor broadcasting as ``[B, H, D, 1]`` against the
-state (``:295``).
+op (there is one implementation and no CPU path).  The result keeps the
+reference's conventions: y has q's dtype, shape and memory order (``:263``),
+the state is not returned (``:297``), and ``decay`` is a float or a tensor
+broadcasting as ``[B, H, D, 1]`` against the state (``:295``).
+
+Input dtypes follow the reference's dispatch on an sm_100 GPU (``:303-328``):
+with ``use_triton=True`` (the model's default, ``config.py:64``) fp16/bf16
+inputs run and fp32 inputs raise ``AssertionError``, because the reference's
+Triton wrapper asserts before its fallback (``:204``); with
+``use_triton=False`` the reference runs its fp32 torch loop, which takes any
+floating dtype, and so does this module: fp32 inputs are rounded to bf16 for
+the tensor-core scan (fp32 products, sums and state, as for bf16 inputs) and y
+comes back in fp32, within the bf16 tolerance (normwise 2e-2) of the
+reference's fp32 result.  Gradients flow through the roundings.
 
 State-update semantics (module attribute ``SEMANTICS``, or the environment
 variable ``KDA_B200_SEMANTICS`` read at import):
@@ -30,9 +39,11 @@ variable ``KDA_B200_SEMANTICS`` read at import):
   (``:8-11``) and Triton kernel (``:134-180``), ``s_t = decay s_{t-1} +
   k_t^T v_t``, with one decay per (batch, head) in [0.125, 1].
 
-Errors: non-fp16/bf16 inputs raise ``AssertionError`` (the reference's
-Triton wrapper asserts the same, ``:204``); CPU tensors raise
-``RuntimeError`` (there is no CPU path).
+Errors: fp32 inputs with ``use_triton=True`` (or through
+``kda_chunked_scan_triton``) raise ``AssertionError`` like the reference
+(``:204``); other dtypes raise ``TypeError``; CPU tensors raise
+``RuntimeError`` (there is no CPU path: the reference would run its torch
+loop on the CPU, this module serves only the B200 kernels).
 
 ``install()`` makes ``import kernels.kda_kernel`` (and an already imported
 ``models.kimi_k3``) resolve to this module, so ``models/kimi_k3.py`` and
@@ -92,12 +103,9 @@ def _decay_arg(decay: Union[float, torch.Tensor], B: int, H: int, D: int):
     return torch.broadcast_to(d, (B, H, D, 1)).squeeze(-1)
 
 
-def kda_chunked_scan_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                            gate: Optional[torch.Tensor] = None, decay: float = 0.99,
-                            chunk_size: int = 64) -> torch.Tensor:
-    """Run the scan on the sm_100a kernels; returns y of shape ``[B, H, T, D]``."""
-    if q.dtype not in (torch.float16, torch.bfloat16):
-        raise AssertionError("KDA sm_100a kernel requires fp16/bf16")
+def _scan16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gate: Optional[torch.Tensor],
+            decay: Union[float, torch.Tensor], chunk_size: int) -> torch.Tensor:
+    """The sm_100a scan on fp16/bf16 inputs, in the semantics ``SEMANTICS`` picks."""
     _validate(q, k, v, gate, chunk_size)
     B, H, T, D = q.shape
     if SEMANTICS == "per_step":
@@ -110,11 +118,36 @@ def kda_chunked_scan_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return y
 
 
+def kda_chunked_scan_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            gate: Optional[torch.Tensor] = None, decay: float = 0.99,
+                            chunk_size: int = 64) -> torch.Tensor:
+    """Run the scan on the sm_100a kernels; returns y of shape ``[B, H, T, D]``.
+
+    Takes fp16/bf16 inputs only, as the reference's wrapper asserts (``:204``)."""
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise AssertionError("KDA sm_100a kernel requires fp16/bf16")
+    return _scan16(q, k, v, gate, decay, chunk_size)
+
+
 def kda_chunked_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                      gate: Optional[torch.Tensor] = None, decay: float = 0.99,
                      chunk_size: int = 64, use_triton: bool = True) -> torch.Tensor:
-    """SimpleTrain's KDA dispatch, served by the sm_100a kernels (``use_triton`` ignored)."""
-    return kda_chunked_scan_triton(q, k, v, gate, decay, chunk_size)
+    """SimpleTrain's KDA dispatch, served by the sm_100a kernels.
+
+    ``use_triton=True``: fp16/bf16 only (fp32 raises ``AssertionError``, as the
+    reference's wrapper does on an sm_100 GPU).  ``use_triton=False``: the
+    reference's torch loop takes fp32 too; fp32 inputs run here on bf16-rounded
+    copies and y is returned in fp32."""
+    if use_triton or q.dtype in (torch.float16, torch.bfloat16):
+        return kda_chunked_scan_triton(q, k, v, gate, decay, chunk_size)
+    if q.dtype != torch.float32:
+        raise TypeError(f"KDA scan takes fp32, fp16 or bf16 inputs, got {q.dtype}")
+    if q.device.type != "cuda":
+        raise RuntimeError("the KDA sm_100a kernels need CUDA tensors (there is no CPU path)")
+    lo = torch.bfloat16
+    y = _scan16(q.to(lo), k.to(lo), v.to(lo), gate.to(lo) if gate is not None else None,
+                decay, chunk_size)
+    return y.to(q.dtype)
 
 
 def install() -> None:

@@ -34,6 +34,15 @@ import torch.nn.functional as F
 from . import kda_kernel
 
 
+def _use_triton(layer) -> bool:
+    """The layer's ``use_triton`` setting: ``cfg.use_triton`` on SimpleTrain's
+    module (``models/kimi_k3.py:117``), the attribute on ``KDALayer``."""
+    cfg = getattr(layer, "cfg", None)
+    if cfg is not None and hasattr(cfg, "use_triton"):
+        return bool(cfg.use_triton)
+    return bool(getattr(layer, "use_triton", True))
+
+
 def fused_forward(self, x: torch.Tensor) -> torch.Tensor:
     """``KimiDeltaAttention.forward`` with one projection GEMM and no host sync: [B, T, D] -> [B, T, D]."""
     B, T, _ = x.shape
@@ -45,7 +54,8 @@ def fused_forward(self, x: torch.Tensor) -> torch.Tensor:
     dt = self._dtype()
     q, k, v, g = (t.transpose(1, 2).to(dt) for t in qkvg)   # [B, H, T, Dh] views
     decay = torch.exp(self.log_decay).clamp(min=1e-3, max=0.999).detach().mean()   # stays on the device
-    o = kda_kernel.kda_chunked_scan(q, k, v, gate=g, decay=decay, chunk_size=self.chunk)   # [B, H, T, Dh]
+    o = kda_kernel.kda_chunked_scan(q, k, v, gate=g, decay=decay, chunk_size=self.chunk,
+                                    use_triton=_use_triton(self))   # [B, H, T, Dh]
     head_scale = torch.exp(self.log_decay).clamp(min=1e-3, max=0.999)
     o = o * head_scale.view(1, H, 1, 1).to(o.dtype)
     return self.o_proj(o.transpose(1, 2).contiguous().view(B, T, H * Dh))
@@ -75,7 +85,8 @@ def unfused_forward(self, x: torch.Tensor) -> torch.Tensor:
     q, k, v, g = (p(x).view(B, T, H, Dh).transpose(1, 2).to(dt)
                   for p in (self.q_proj, self.k_proj, self.v_proj, self.g_proj))
     decay = float(torch.exp(self.log_decay).clamp(min=1e-3, max=0.999).detach().mean().item())
-    o = kda_kernel.kda_chunked_scan(q, k, v, gate=g, decay=decay, chunk_size=self.chunk)
+    o = kda_kernel.kda_chunked_scan(q, k, v, gate=g, decay=decay, chunk_size=self.chunk,
+                                    use_triton=_use_triton(self))
     head_scale = torch.exp(self.log_decay).clamp(min=1e-3, max=0.999)
     o = o * head_scale.view(1, H, 1, 1).to(o.dtype)
     return self.o_proj(o.transpose(1, 2).contiguous().view(B, T, H * Dh))
@@ -88,9 +99,11 @@ class KDALayer(nn.Module):
     way, running ``fused_forward``."""
 
     def __init__(self, d_model: int, n_heads: int, d_head: int, chunk_size: int = 64,
-                 decay_base: float = 0.99, dtype: torch.dtype = torch.bfloat16):
+                 decay_base: float = 0.99, dtype: torch.dtype = torch.bfloat16,
+                 use_triton: bool = True):
         super().__init__()
         self.n_heads, self.d_head, self.chunk = n_heads, d_head, chunk_size
+        self.use_triton = use_triton
         self.inner = n_heads * d_head
         self._dt = dtype
         self.q_proj = nn.Linear(d_model, self.inner, bias=False)

@@ -22,6 +22,7 @@ variant has 8 heads of 64, 1b has 10 heads of 128, 7b 24 heads of 128 and 10b
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import Dict, Optional
 
@@ -117,3 +118,46 @@ def make_inputs(w: Workload, seed: int = 0, device: Optional[str] = None) -> Dic
         out = {n: (t.to(device) if t is not None else None) for n, t in out.items()}
         # .to() on a strided view keeps the [B, T, H, D] memory order
     return out
+
+
+def layer_params(d_model: int, n_heads: int, d_head: int, seed: int = 0) -> Dict[str, torch.Tensor]:
+    """Seeded fp32 parameters of one KDA layer, keyed by SimpleTrain's names.
+
+    ``KimiDeltaAttention`` (``models/kimi_k3.py:81-89``) holds ``q_proj``,
+    ``k_proj``, ``v_proj``, ``g_proj`` and ``o_proj`` (bias-free Linear) and a
+    per-head ``log_decay``.  Weights are N(0, 1/fan_in); the gate projection is
+    drawn too (the layer zero-initialises it, ``:92``, which would make every
+    output zero); ``log_decay = log(U(0.9, 0.99))`` per head, so the scan's mean
+    decay and the per-head scale (``:105-122``) both vary.  Drawn in the fixed
+    order q, k, v, g, o, log_decay from one CPU generator.
+    """
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(seed)
+    inner = n_heads * d_head
+
+    def linear(n_out: int, n_in: int) -> torch.Tensor:
+        return torch.randn(n_out, n_in, generator=gen, dtype=torch.float32) * n_in ** -0.5
+
+    p = {f"{n}.weight": linear(inner, d_model) for n in ("q_proj", "k_proj", "v_proj", "g_proj")}
+    p["o_proj.weight"] = linear(d_model, inner)
+    p["log_decay"] = torch.log(torch.rand(n_heads, generator=gen, dtype=torch.float32) * 0.09 + 0.9)
+    return p
+
+
+def layer_input(B: int, T: int, d_model: int, seed: int = 1):
+    """Seeded layer input x and upstream gradient dy, both ``[B, T, d_model]`` fp32 N(0, 1)."""
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(seed)
+    x = torch.randn(B, T, d_model, generator=gen, dtype=torch.float32)
+    dy = torch.randn(B, T, d_model, generator=gen, dtype=torch.float32)
+    return x, dy
+
+
+def sketch_vectors(n_out: int, n_in: int, seed: int):
+    """Seeded N(0, 1) probe vectors (r_out [n_out], r_in [n_in]) for a matrix sketch
+    ``(W r_in, r_out W)``: two projections that compare a weight gradient without
+    storing it."""
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(seed)
+    return (torch.randn(n_out, generator=gen, dtype=torch.float64),
+            torch.randn(n_in, generator=gen, dtype=torch.float64))

@@ -68,6 +68,68 @@ def test_seeded_cpu_workload_matches_reference(golden_dir):
     assert max_rel((yc * yc).sum(dim=(3, 4)), f["chunk_sumsq"]) <= 1e-5
 
 
+@pytest.mark.parametrize("name,tol", [("cor_d128_f32.pt", 1e-5), ("cor_d128_bf16.pt", 1e-2)])
+def test_corrected_matches_reference_kt_v_fixture(golden_dir, name, tol):
+    """The corrected (K^T V) mode against the reference's own function with only
+    its :294 einsum changed (D=128, ragged tail, float and per-channel decay)."""
+    f = _load(golden_dir, name)
+    C = f["chunk"]
+    res = _grads(lambda q, k, v, g, d: chunk_scan(q, k, v, g, d, C, mode="corrected")[0],
+                 f["q"], f["k"], f["v"], f["g"], f["decay"], f["dy"])
+    assert f["q"].shape[-1] == 128 and f["q"].shape[2] % C != 0
+    for key in ("y", "dq", "dk", "dv", "dg") + (("ddecay",) if "ddecay" in f else ()):
+        assert res[key].dtype == f[key].dtype, key
+        assert max_rel(res[key], f[key]) <= tol, (key, max_rel(res[key], f[key]))
+
+
+def test_corrected_fixture_generator_changes_one_line():
+    """The generator's one-line change, checked on a synthetic source: exactly the
+    state-update einsum differs, so the D=128 fixtures run the reference's code."""
+    import types
+
+    from tests.golden.make_golden import CORRECTED_KV, LITERAL_KV, corrected_reference
+    src = ("import torch\n"
+           "def _kda_chunked_scan_torch(kc, vc):\n"
+           "    s = 0\n"
+           f"    full_kv = {LITERAL_KV}     # [B,H,D,D]\n"
+           "    return full_kv\n")
+    mod = types.ModuleType("fake_kda")
+    mod.__file__ = "fake_kda.py"
+    exec(compile(src, "fake_kda.py", "exec"), mod.__dict__)
+    import inspect
+    import linecache
+    linecache.cache["fake_kda.py"] = (len(src), None, src.splitlines(True), "fake_kda.py")
+    assert "bhpq" in inspect.getsource(mod._kda_chunked_scan_torch)
+    fn = corrected_reference(mod)
+    kc = torch.randn(1, 1, 5, 3)
+    vc = torch.randn(1, 1, 5, 3)
+    assert torch.allclose(fn(kc, vc), kc.transpose(-1, -2) @ vc)
+    assert CORRECTED_KV != LITERAL_KV
+
+
+@pytest.mark.parametrize("name,mode", [("layer_100m.pt", "literal"), ("layer_1b.pt", "corrected")])
+def test_layer_fixture_matches_oracle_layer(golden_dir, name, mode):
+    """SimpleTrain's KimiDeltaAttention output and gradients (fp32, CPU) against the
+    oracle's restatement of the layer on the same seeded parameters and input."""
+    from oracle.kda_oracle import layer_forward
+    from simpletrain_b200.workloads import layer_input, layer_params, sketch_vectors
+    f = _load(golden_dir, name)
+    params = {n: p.requires_grad_(True) for n, p in
+              layer_params(f["d_model"], f["n_heads"], f["d_head"], f["seed_params"]).items()}
+    x, dy = layer_input(f["B"], f["T"], f["d_model"], f["seed_x"])
+    x.requires_grad_(True)
+    y = layer_forward(params, x, f["n_heads"], f["d_head"], f["chunk"], mode)
+    (y * dy).sum().backward()
+    assert max_rel(y, f["y"]) <= 1e-5
+    assert max_rel(x.grad, f["dx"]) <= 1e-5
+    assert max_rel(params["log_decay"].grad, f["dlog_decay"]) <= 1e-5
+    for pname, sk in f["grad_sketches"].items():
+        gd = params[pname].grad.double()
+        r_out, r_in = sketch_vectors(gd.shape[0], gd.shape[1], sk["seed"])
+        assert max_rel(gd @ r_in, sk["W_r_in"]) <= 1e-5, pname
+        assert max_rel(r_out @ gd, sk["r_out_W"]) <= 1e-5, pname
+
+
 def test_literal_fails_like_reference_at_d128(golden_dir):
     f = _load(golden_dir, "d128_error.pt")
     q = torch.randn(1, 1, 128, 128)
