@@ -25,6 +25,9 @@ copies in run while this one's results come back), with two sets of result
 buffers used in turn, so a call's results stay valid until the second
 submission after it, which first waits for it.  A submitted call's host
 inputs must stay unchanged until its ``wait()`` returns.
+
+``ShardedHostScan`` does the same for one rank's shard of a problem split over
+several GPUs (``sharding.ShardedScan``), pipelining whole steps.
 """
 from __future__ import annotations
 
@@ -35,7 +38,7 @@ from torch import Tensor
 
 from .ops import MODE_CORRECTED, MODE_LITERAL, MODE_PER_STEP, decay_as_bhd, per_step_decay
 
-__all__ = ["HostScan", "Pending"]
+__all__ = ["HostScan", "Pending", "ShardedHostScan"]
 
 _DTYPES = (torch.bfloat16, torch.float16)
 
@@ -255,3 +258,96 @@ class HostScan:
         pending = Pending(dict(ho), finished)
         self._pending[turn] = pending
         return pending
+
+
+class ShardedHostScan:
+    """One rank's shard of a sharded scan (``sharding.ShardedScan``), fed from
+    and returned to host memory, with consecutive steps pipelined.
+
+    ``submit(pieces)`` takes this rank's pieces as host tensors -- the dicts
+    ``ShardedScan.load`` makes, from pinned host inputs -- copies them to the
+    device on a copy-in stream, runs the forward (and the backward when the
+    pieces carry ``dy``) with the scan's exchanges on a compute stream, and
+    copies every result back to pinned host buffers on a copy-out stream.  It
+    returns at once with a ``Pending``; device inputs and host results come in
+    two sets used in turn, so step i+1's copies in run while step i computes
+    and step i-1's results come back, and the two PCIe directions overlap.
+    Results: per piece a dict with ``y``, ``final_state`` and, with ``dy``,
+    ``dq``, ``dk``, ``dv``, ``dg``, ``ddecay`` (a tensor decay), ``ds0`` (a
+    piece that holds the stream's initial state).  A call's results stay
+    valid until the second submission after it, which first waits for it.
+    All ranks must submit the same number of steps (the exchanges are
+    collectives).
+    """
+
+    def __init__(self, scan, device: Optional[Union[int, str, torch.device]] = None,
+                 need_ddecay: bool = True, need_ds0: bool = True):
+        self.scan = scan
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.need = (need_ddecay, need_ds0)
+        self._streams = [torch.cuda.Stream(device=self.device) for _ in range(3)]
+        self._dev = [None, None]       # device inputs per buffer set
+        self._host = [None, None]      # pinned host results per buffer set
+        self._busy = [None, None]      # per set: the event after which its device inputs are free
+        self._pending = [None, None]
+        self._turn = 0
+
+    @staticmethod
+    def _to_device_like(piece, dev):
+        out = {}
+        for n, t in piece.items():
+            out[n] = (torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=dev)
+                      if torch.is_tensor(t) else t)
+        return out
+
+    def submit(self, pieces) -> Pending:
+        s_in, s_run, s_out = self._streams
+        caller = torch.cuda.current_stream(self.device)
+        turn = self._turn
+        self._turn ^= 1
+        if self._pending[turn] is not None:
+            self._pending[turn].wait()
+        if self._dev[turn] is None:
+            self._dev[turn] = [self._to_device_like(p, self.device) for p in pieces]
+        dev = self._dev[turn]
+        with torch.cuda.stream(s_in):
+            s_in.wait_stream(caller)
+            if self._busy[turn] is not None:
+                s_in.wait_event(self._busy[turn])
+            for hp, dp in zip(pieces, dev):
+                for n, t in hp.items():
+                    if torch.is_tensor(t):
+                        dp[n].copy_(t, non_blocking=True)
+            arrived = torch.cuda.Event()
+            arrived.record(s_in)
+        with torch.cuda.stream(s_run), torch.inference_mode():
+            s_run.wait_event(arrived)
+            outs = self.scan.forward(dev)
+            if dev and dev[0].get("dy") is not None:
+                grads = self.scan.backward(dev, *self.need)
+                outs = [dict(o, **g) for o, g in zip(outs, grads)]
+            outs = [{n: t for n, t in o.items() if not (n == "final_state" and not p.ends)}
+                    for o, p in zip(outs, self.scan.pieces)]
+            done = torch.cuda.Event()
+            done.record(s_run)
+        self._busy[turn] = done
+        if self._host[turn] is None:
+            self._host[turn] = [{n: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for n, t in o.items()}
+                                for o in outs]
+        host = self._host[turn]
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            for o, ho in zip(outs, host):
+                for n, t in o.items():
+                    t.record_stream(s_out)
+                    ho[n].copy_(t, non_blocking=True)
+            finished = torch.cuda.Event()
+            finished.record(s_out)
+        pend = Pending(host, finished)
+        self._pending[turn] = pend
+        return pend
+
+    @staticmethod
+    def nbytes(pieces) -> int:
+        """Bytes of the tensors in a list of piece dicts (inputs or results)."""
+        return sum(t.numel() * t.element_size() for p in pieces for t in p.values() if torch.is_tensor(t))
