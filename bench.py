@@ -7,9 +7,20 @@
 
 One step = one forward + backward pass of the KDA scan over one batch of the
 workload (default: the 1b-variant shape B=16, H=10, T=2048, D=128, chunk 64,
-bf16).  Work shards by (batch, head): every rank runs its own full batch of
-independent (b, h) units with no collective on the data path (weak scaling);
-``value`` = tokens all ranks processed / max-over-ranks device time.
+bf16).  With N ranks the one global problem is sharded (``--scaling strong``,
+the default): the stream-major (stream, chunk) sequence is cut into N balanced
+ranges (``simpletrain_b200.sharding``); whole streams need no communication,
+and a stream that straddles two ranks (the 10b shape: 28 heads over 8 GPUs)
+is split in time with one small all_gather of carried states per direction.
+``value`` = the problem's tokens / the max-over-ranks device time per step.
+``--scaling weak`` gives every rank its own full batch instead.
+
+Each rank's step is captured once in a CUDA graph and replayed (the step's
+launches cost more host time than a rank's share of the work takes on the
+device at 8 GPUs).  Per-kernel device times come from the library's own
+CUDA-event tracer (``kda_trace_start``) over an eager pass of the same steps
+right after the timed region.  At N > 1 the ranks' results are gathered on
+rank 0 after timing and checked against a single-GPU run of the whole problem.
 
 Prints one JSON line (rank 0).
 """
@@ -35,6 +46,14 @@ from simpletrain_b200.workloads import WORKLOADS, make_inputs  # noqa: E402
 METRIC = "KDA fwd+bwd tokens/s"
 UNIT = "tokens/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+DATA = ("synthetic (seeded; q,k L2-normalised N(0,1), v N(0,1), g sigmoid(N(0,1)), "
+        "decay sigmoid(N(3,1)) per key channel (N(4,1) at 10b, with an N(0,0.02) initial state))")
+
+# Algorithmic HBM bytes of each kernel per token-head, in units of D x element
+# size: the tensors it must read and write once.  fwd: q,k,v,g in, y out; the
+# backward's forward-direction pass: q,k,v,g,dy in, dq,dg and dO = dy*g (handed
+# to the second pass) out; its reverse pass: q,k,v,dO in, dk,dv out.
+KERNEL_BYTES_D = {"fwd_tc_kernel": 5, "bwd_fwddir_tc_kernel": 8, "bwd_revdir_tc_kernel": 6}
 
 
 def load_peaks():
@@ -46,28 +65,30 @@ def load_peaks():
     return dict(PEAKS_FALLBACK, source="fallback")
 
 
-def algorithmic(w, rank_heads=None):
-    """Algorithmic HBM bytes and flops per launch-group (per rank, per step).
+def semantics(args, w):
+    """(op mode, decay kind, need d(decay), label) the workload runs in.
 
-    Per token-head with chunk C: forward reads q,k,v,g and writes y (10*D bytes
-    in bf16) and costs 4CD + 4D^2 flops; backward reads q,k,v,g,dy and writes
-    dq,dk,dv,dg (18*D bytes) and costs 8CD + 8D^2 flops.  Plus the fp32 DxD
-    state once per (b, h) per direction.
-    """
-    B, H, T, D, C = w.B, w.H, w.T, w.D, w.chunk
-    th = B * H * T
-    bh = B * H
-    esz = torch.finfo(w.dtype).bits // 8
-    fwd_bytes = th * 5 * D * esz + bh * D * D * 4
-    bwd_bytes = th * 9 * D * esz + bh * D * D * 4 + bh * D * 4
-    return {
-        "fwd": {"bytes": fwd_bytes, "flops": th * (4 * C * D + 4 * D * D)},
-        "bwd": {"bytes": bwd_bytes, "flops": th * (8 * C * D + 8 * D * D)},
-    }
+    D == chunk (the 100m variant): the reference's own literal K V^T update with
+    a float decay, as SimpleTrain's model calls it (models/kimi_k3.py:109-118).
+    Otherwise the K^T V update with a per-key-channel decay and its gradient;
+    --per-step: the per-token recurrence with one decay per head."""
+    if args.per_step:
+        return 2, "head", False, "per-step decay (one per head)"
+    if w.D == w.chunk and not args.corrected:
+        return 1, "float", False, "literal K V^T update (the reference's own at D == chunk), float decay"
+    return 0, "channel", w.backward, "K^T V update, chunk-constant per-channel decay (with its gradient)"
+
+
+def decay_input(kind, decay):
+    if kind == "head":
+        return decay[:, :1].contiguous()            # [H, 1]: the first channel's, per head
+    if kind == "float":
+        return float(decay.mean())                  # the model's float(decay.mean())
+    return decay                                    # [H, D]
 
 
 # --------------------------------------------------------------------------- #
-# clocks during the timed region
+# clocks during warm-up and the timed region
 # --------------------------------------------------------------------------- #
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -88,8 +109,6 @@ class ClockSampler:
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
-            # nvidia-smi takes a moment to start: wait (at most 3 s) for its first
-            # sample so that even a short timed region is covered
             t0 = time.time()
             while os.path.getsize(self.path) == 0 and self.proc.poll() is None and time.time() - t0 < 3.0:
                 time.sleep(0.02)
@@ -99,12 +118,14 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.fh.close()
+            if self.proc.poll() is None:
+                self.proc.terminate()
+                try:
+                    self.proc.wait(timeout=5)
+                except Exception:
+                    self.proc.kill()
+            if not self.fh.closed:
+                self.fh.close()
 
     def summary(self):
         if self.proc is None or self.path is None:
@@ -124,70 +145,120 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None,
+                "covers": "warm-up and timed region"}
 
 
 # --------------------------------------------------------------------------- #
 # our arm
 # --------------------------------------------------------------------------- #
-def traffic_from_profiles(w, kernel: str):
-    """DRAM bytes per launch-group from a committed ncu summary, scaled by units."""
+def traffic_per_token_head(kernel: str, D: int):
+    """DRAM bytes per token-head of one kernel from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "dram_traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as fh:
-        d = json.load(fh)
-    ent = d.get(f"{kernel}:D{w.D}")
-    if not ent:
-        return None
-    return ent["bytes_per_token_head"] * w.B * w.H * w.T
+        ent = json.load(fh).get(f"{kernel}:D{D}")
+    return ent["bytes_per_token_head"] if ent else None
+
+
+def global_inputs(w, dev, rank, world, seed):
+    """The seeded global problem on every rank's device: drawn on the host by
+    rank 0 (the same bytes the tests use) and broadcast over NCCL."""
+    import torch.distributed as dist
+    if rank == 0:
+        inp = make_inputs(w, seed=seed, device=dev)
+    else:
+        bthd = (w.B, w.T, w.H, w.D)
+        inp = {n: torch.empty(bthd, dtype=w.dtype, device=dev).transpose(1, 2)
+               for n in ("q", "k", "v", "g") + (("dy",) if w.backward else ())}
+        inp["decay"] = torch.empty(w.H, w.D, dtype=torch.float32, device=dev)
+        inp["s0"] = torch.empty(w.B, w.H, w.D, w.D, dtype=torch.float32, device=dev) if w.s0_std > 0 else None
+        if not w.backward:
+            inp["dy"] = None
+    if world > 1:
+        for n in ("q", "k", "v", "g", "dy", "decay", "s0"):
+            t = inp.get(n)
+            if t is not None:
+                # [B, H, T, D] views over [B, T, H, D] memory: broadcast the memory
+                base = t.transpose(1, 2) if t.dim() == 4 and n != "s0" else t
+                dist.broadcast(base, 0)
+    return inp
 
 
 def run_ours(args, w, rank, world, local_rank):
+    clk = ClockSampler(local_rank)
+    try:
+        return _run_ours(args, w, rank, world, local_rank, clk)
+    finally:
+        clk.__exit__(None, None, None)
+
+
+def _run_ours(args, w, rank, world, local_rank, clk):
     import torch.distributed as dist
 
     import simpletrain_b200.ops  # noqa: F401  (loads the ops)
     from simpletrain_b200 import _ffi
-    from simpletrain_b200.ops import device_status, kda_chunk
+    from simpletrain_b200.ops import device_status
+    from simpletrain_b200.sharding import ShardedScan, cuda_scan_fns, nccl_exchange
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    inp = make_inputs(w, seed=rank, device=dev)
-    q, k, v, g, dy, decay, s0 = (inp[n] for n in ("q", "k", "v", "g", "dy", "decay", "s0"))
-    B, H, T, D = w.B, w.H, w.T, w.D
-    if args.per_step:
-        # per-token decay, one value per head (the first channel's)
-        mode, need_dd = 2, False
-        dec = decay[:, :1].expand(B, H, D)
-    else:
-        mode, need_dd = 0, True
-        dec = decay.expand(B, H, D)
-    fwd = torch.ops.kda_b200.chunk_fwd
-    bwd = torch.ops.kda_b200.chunk_bwd
+    strong = args.scaling == "strong"
+    mode, dkind, need_dd, sem_label = semantics(args, w)
+    clk.__enter__()          # sampled from the warm-up to the end of the timed region
 
-    # the ops are called directly (their backward explicitly): no autograd
-    # bookkeeping, which would add a Python layer to every call
-    inference = torch.inference_mode()
-    inference.__enter__()
+    if strong:
+        inp = global_inputs(w, dev, rank, world, seed=0)
+    else:
+        inp = make_inputs(w, seed=rank, device=dev)
+    decay = decay_input(dkind, inp["decay"])
+    B, H, T, D = w.B, w.H, w.T, w.D
+    fwd, bwd = cuda_scan_fns(w.chunk, mode)
+    sworld, srank = (world, rank) if strong else (1, 0)
+    sc = ShardedScan(B, H, T, D, w.chunk, sworld, srank, fwd=fwd, bwd=bwd,
+                     exchange=nccl_exchange() if sworld > 1 else None)
+    x = sc.load({"q": inp["q"], "k": inp["k"], "v": inp["v"], "g": inp["g"], "dy": inp["dy"],
+                 "decay": decay, "s0": inp["s0"]})
+    need_ds0 = inp["s0"] is not None
+    rank_token_heads = sum(p.nstreams * (min(T, p.c1 * w.chunk) - p.c0 * w.chunk) for p in sc.pieces)
 
     def step():
-        y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, mode, True)
-        if w.backward:
-            return bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, mode, need_dd, s0 is not None)
-        return y
+        outs = sc.forward(x)
+        grads = sc.backward(x, need_dd, need_ds0) if w.backward else None
+        return outs, grads
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 1)):
-        step()
-    torch.cuda.synchronize()
+    # warm-up (eager, on a side stream as graph capture requires), then capture
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(stream)
+    with torch.inference_mode():
+        with torch.cuda.stream(side):
+            for _ in range(max(args.warmup, 1)):
+                step()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = None
+        if not args.eager:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            run = graph.replay
+        else:
+            run = step
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+
     steps = args.steps
     if steps is None:
         t0 = time.perf_counter()
         for _ in range(3):
-            step()
+            run()
         torch.cuda.synchronize()
         per = (time.perf_counter() - t0) / 3
         steps = int(min(5000, max(10, 3.0 / max(per, 1e-6))))
@@ -196,66 +267,85 @@ def run_ours(args, w, rank, world, local_rank):
             dist.all_reduce(t, op=dist.ReduceOp.MIN)
             steps = int(t.item())
 
-    stream = torch.cuda.current_stream(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _ffi.launch_count()
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(dev.index) as clk:
+    with torch.inference_mode():
         start.record(stream)
-        for i in range(steps):
-            e0, e1, e2 = ev[i]
-            e0.record(stream)
-            y, sT = fwd(q, k, v, g, dec, 0.0, s0, w.chunk, mode, True)
-            e1.record(stream)
-            if w.backward:
-                bwd(q, k, v, g, dy, dec, 0.0, s0, None, None, w.chunk, mode, need_dd, s0 is not None)
-            e2.record(stream)
+        for _ in range(steps):
+            run()
         end.record(stream)
         torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
     barrier()
-    launches = _ffi.launch_count() - launches0
     ms = start.elapsed_time(end)
-    fwd_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1, _ in ev)
-    bwd_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev) if w.backward else 0.0
-    t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    graphed_launches = _ffi.launch_count() - launches0   # launches issued from the host (0 when replayed)
+
+    # ---- per-kernel device times: the library's event tracer, eager pass ----------
+    trace_steps = min(steps, 50)
+    with torch.inference_mode():
+        barrier()
+        with _ffi.KernelTrace(max_launches=16 * trace_steps + 16) as tr:
+            for _ in range(trace_steps):
+                step()
+            torch.cuda.synchronize()
+        barrier()
+    per_kernel = tr.per_kernel()
+    kernels_per_step = sum(c for c, _ in per_kernel.values()) / trace_steps
+    launches = graphed_launches if graph is None else int(round(kernels_per_step * steps))
+
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
-    inference.__exit__(None, None, None)
+    ms = float(t.item())
     status = device_status(dev)
     if status:
         raise RuntimeError(f"device-side KDA status {status}")
 
-    tokens_per_step = world * B * T
+    tokens_per_step = (B * T) if strong else world * B * T
     value = tokens_per_step * steps / (ms / 1e3)
 
-    # ---- roofline of the dominant launch group ---------------------------------
+    # ---- roofline of the dominant kernel -----------------------------------------
     peaks = load_peaks()
-    alg = algorithmic(w)
-    groups = {"fwd": fwd_ms}
-    if w.backward:
-        groups["bwd"] = bwd_ms
-    dom = max(groups, key=groups.get)
-    achieved = alg[dom]["bytes"] / (groups[dom] / 1e3) / 1e9
-    traffic = traffic_from_profiles(w, dom)
+    esz = torch.finfo(w.dtype).bits // 8
     kernels = {}
-    for name, t_ms in groups.items():
-        kernels[name] = {"ms": round(t_ms, 4),
-                         "GB_s": round(alg[name]["bytes"] / (t_ms / 1e3) / 1e9, 1),
-                         "TFLOP_s": round(alg[name]["flops"] / (t_ms / 1e3) / 1e12, 1)}
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": traffic, "kernel": f"kda_{dom}",
-                "peak_source": peaks["source"],
-                "tensor_frac": round(alg[dom]["flops"] / (groups[dom] / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
-                "step_frac": round(sum(alg[n]["bytes"] for n in groups) / (ms / steps / 1e3) / 1e9
-                                   / peaks["hbm_gbs"], 4)}
+    for name, (count, mean_ms) in sorted(per_kernel.items()):
+        ent = {"launches_per_step": round(count / trace_steps, 3), "ms": round(mean_ms, 5),
+               "share": round(count * mean_ms / sum(c * m for c, m in per_kernel.values()), 4)}
+        if name in KERNEL_BYTES_D:
+            nbytes = rank_token_heads * KERNEL_BYTES_D[name] * D * esz
+            ent["algorithmic_bytes"] = nbytes
+            ent["GB_s"] = round(nbytes / (mean_ms / 1e3) / 1e9, 1)
+            ent["frac_hbm"] = round(nbytes / (mean_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)
+        kernels[name] = ent
+    dom = max(per_kernel, key=lambda n: per_kernel[n][0] * per_kernel[n][1])
+    dbytes = kernels[dom].get("algorithmic_bytes")
+    dms = per_kernel[dom][1]
+    tph = traffic_per_token_head(dom, D)
+    step_bytes = rank_token_heads * (14 if w.backward else 5) * D * esz     # q,k,v,g,y (+dy,dq,dk,dv,dg)
+    step_flops = rank_token_heads * ((12 if w.backward else 4) * w.chunk * D + (12 if w.backward else 4) * D * D)
+    per_step_s = ms / steps / 1e3
+    roofline = {"bound": "hbm", "kernel": dom,
+                "achieved": round(dbytes / (dms / 1e3) / 1e9, 1) if dbytes else None,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(dbytes / (dms / 1e3) / 1e9 / peaks["hbm_gbs"], 4) if dbytes else None,
+                "traffic": round(tph * rank_token_heads) if tph else None,
+                "algorithmic_bytes": dbytes, "peak_source": peaks["source"],
+                "kernel_ms": round(dms, 5),
+                "kernel_times": f"CUDA events around each launch (library tracer), eager pass of {trace_steps} steps "
+                                "right after the timed region",
+                "step_frac_hbm": round(step_bytes / per_step_s / 1e9 / peaks["hbm_gbs"], 4),
+                "step_frac_tensor": round(step_flops / per_step_s / 1e12 / peaks["bf16_tflops"], 4),
+                "step_bytes_per_rank": step_bytes}
 
-    # ---- end to end through the public API with host buffers --------------------
-    e2e = run_e2e(args, w, rank, world, dev, inp) if not args.no_e2e else None
+    # ---- the sharded result against one GPU's ------------------------------------
+    check = run_check(args, w, sc, x, inp, decay, mode, need_dd, rank, world, dev) if strong and world > 1 else None
+
+    # ---- end to end through the host-buffer API ----------------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, w, sc, x, rank, world, dev, need_dd, need_ds0, tokens_per_step)
 
     # ---- CPU baseline (rank 0, N = 1) ----------------------------------------------
     cpu = None
@@ -263,67 +353,116 @@ def run_ours(args, w, rank, world, local_rank):
         cpu = {"unavailable": "the reference has no CPU implementation of per-step decay "
                               "(only its never-launched Triton kernel describes it)"}
     elif rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(w, budget_s=args.cpu_seconds)
+        cpu = cpu_baseline(w, mode, budget_s=args.cpu_seconds)
 
+    launch_mode = "CUDA graph replay" if graph is not None else "eager"
+    if graph is not None:
+        del graph           # holds NCCL calls at N > 1: released before the process group
     return {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(ms / steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f16",
-        "data": "synthetic (seeded; q,k L2-normalised N(0,1), v N(0,1), g sigmoid(N(0,1)), "
-                "per-channel decay sigmoid(N(3,1)))",
-        "config": dict(w.describe(), global_batch=w.B * world, seq_len=w.T,
-                       semantics="per-step decay (one per head)" if args.per_step else "chunk-constant decay",
-                       parallelism=f"(batch,head) shards, {world} rank(s), no data-path collective",
-                       l2="inputs larger than L2 (no flush needed)"),
-        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": launches, "clocks": clk.summary(),
+        "scaling": "strong" if strong else "weak", "vs_baseline": None,
+        "dtype": "bf16" if w.dtype == torch.bfloat16 else "f16",
+        "data": DATA,
+        "config": config_dict(w, world, strong, sem_label, args),
+        "shard": {"pieces": [[p.s0, p.s1, p.c0, p.c1] for p in sc.pieces], "split_streams": sc.split,
+                  "token_heads_rank0": rank_token_heads},
+        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "check": check,
+        "gpu_launches": launches, "launch_mode": launch_mode,
+        "clocks": clk.summary(),
     }
 
 
-def run_e2e(args, w, rank, world, dev, inp):
-    """Same metric through the public host-buffer API (``HostScan``): each step
-    copies its inputs (q, k, v, g, dy, decay, initial state) from pinned host
-    memory to the device and its results (y, final state, dq, dk, dv, dg,
-    d_decay, d_initial_state) back, inside the timed region; the batch is
-    pipelined in slices so both copy directions overlap the kernels, and each
-    step is submitted before the previous step's results are awaited, so one
-    step's copies in overlap the previous step's copies out."""
+def config_dict(w, world, strong, sem_label, args):
+    return dict(w.describe(), global_batch=w.B if strong else w.B * world, seq_len=w.T,
+                semantics=sem_label,
+                parallelism=(f"one problem sharded over {world} rank(s) by (stream, chunk) ranges; "
+                             "time-split streams exchange one carried state per direction"
+                             if strong else f"(batch,head) weak scaling, {world} rank(s), no data-path collective"),
+                l2="inputs larger than L2 (no flush needed)")
+
+
+def run_check(args, w, sc, x, inp, decay, mode, need_dd, rank, world, dev):
+    """Gather every rank's results on rank 0 and compare them with one GPU's run of
+    the whole problem: normwise max|x - ref| / max|ref| per tensor, within 1e-3
+    for the fp32 final state and 2e-2 for y and every gradient."""
+    from simpletrain_b200.sharding import ShardedScan, cuda_scan_fns
+
+    B, H, T, D = w.B, w.H, w.T, w.D
+    need_ds0 = inp["s0"] is not None
+    f32 = torch.float32
+    shapes = {"y": ((B, H, T, D), w.dtype), "final_state": ((B, H, D, D), f32)}
+    if w.backward:
+        shapes.update({n: ((B, H, T, D), w.dtype) for n in ("dq", "dk", "dv", "dg")})
+        if need_dd:
+            shapes["ddecay"] = ((B, H, D), f32)
+        if need_ds0:
+            shapes["ds0"] = ((B, H, D, D), f32)
+
+    def run(scan, xs):
+        with torch.inference_mode():
+            outs = scan.forward(xs)
+            if w.backward:
+                grads = scan.backward(xs, need_dd, need_ds0)
+                outs = [dict(o, **g) for o, g in zip(outs, grads)]
+            return outs
+
+    def assemble(scan, outs):
+        return scan.assemble(outs, shapes, dev)
+
+    res = assemble(sc, run(sc, x))
+    if rank != 0:
+        return None
+    one = ShardedScan(B, H, T, D, w.chunk, 1, 0, *cuda_scan_fns(w.chunk, mode))
+    xo = one.load({"q": inp["q"], "k": inp["k"], "v": inp["v"], "g": inp["g"], "dy": inp["dy"],
+                   "decay": decay, "s0": inp["s0"]})
+    ref = assemble(one, run(one, xo))
+    errs = {}
+    for n in shapes:
+        a, b = res[n].double(), ref[n].double()
+        den = b.abs().max().item()
+        errs[n] = (a - b).abs().max().item() / den if den > 0 else float((a - b).abs().max().item())
+    tol = {n: (1e-3 if n == "final_state" else 2e-2) for n in errs}
+    return {"against": "one GPU running the whole problem (same kernels, same inputs)",
+            "max_rel": {n: float(f"{e:.3e}") for n, e in errs.items()},
+            "ok": all(errs[n] <= tol[n] for n in errs)}
+
+
+def run_e2e(args, w, sc, x, rank, world, dev, need_dd, need_ds0, tokens_per_step):
+    """The same metric through the host-buffer API (``ShardedHostScan``): every
+    step copies this rank's pieces (q, k, v, g, dy, decay, initial state) from
+    pinned host memory to the device and every result back, inside the timed
+    region; consecutive steps are pipelined so the two copy directions overlap
+    each other and the kernels.  Then the copy floor: the same bytes moved by
+    all ranks at once with nothing else running."""
     import torch.distributed as dist
 
-    from simpletrain_b200.host_stream import HostScan
+    from simpletrain_b200.host_stream import ShardedHostScan
 
-    names = ["q", "k", "v", "g", "dy"] if w.backward else ["q", "k", "v", "g"]
+    def pinned(t):
+        if not torch.is_tensor(t):
+            return t
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        return h
 
-    def pinned_like(t):
-        return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device="cpu", pin_memory=True)
-
-    extra = ["decay"] + (["s0"] if inp["s0"] is not None else [])
-    host = {n: pinned_like(inp[n]) for n in names + extra}
-    for n in names + extra:
-        host[n].copy_(inp[n])
-    # per-step: one decay per head (the first channel's), not differentiated
-    decay = host["decay"][:, 0].contiguous() if args.per_step else host["decay"]
-    scan = HostScan(dev, slices=args.e2e_slices, chunk_size=w.chunk, per_step=args.per_step)
+    host = [{n: pinned(t) for n, t in p.items()} for p in x]
+    runner = ShardedHostScan(sc, dev, need_dd, need_ds0)
+    h2d = ShardedHostScan.nbytes(host)
     steps = args.e2e_steps
-    h2d = sum(host[n].numel() * host[n].element_size() for n in names + ["s0"] if n in host)
-    h2d += decay.numel() * decay.element_size()
-    d2h = 0
 
     def run(n):
-        """n steps, each submitted before the previous one's results are awaited."""
-        nonlocal d2h
-        pend = None
+        pend = [None]
+        out = None
         for i in range(n + 1):
-            nxt = None
-            if i < n:
-                nxt = scan.submit(host["q"], host["k"], host["v"], host["g"], decay, dy=host.get("dy"),
-                                  initial_state=host.get("s0"))
-            if pend is not None:
-                out = pend.wait()
-                d2h = sum(o.numel() * o.element_size() for o in out.values())
-            pend = nxt
+            nxt = runner.submit(host) if i < n else None
+            if pend[0] is not None:
+                out = pend[0].wait()
+            pend[0] = nxt
+        return out
 
-    run(2)
+    out = run(2)
+    d2h = ShardedHostScan.nbytes(out)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -334,65 +473,99 @@ def run_e2e(args, w, rank, world, dev, inp):
     b.record(stream)     # after the last step's results were awaited on the host
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    floor_ms = copy_floor(h2d, d2h, dev, world)
+    t = torch.tensor([ms, floor_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    return {"value": round(world * w.B * w.T * steps / (ms / 1e3), 1), "unit": UNIT,
+    ms, floor_ms = (float(v) for v in t.tolist())
+    return {"value": round(tokens_per_step * steps / (ms / 1e3), 1), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
-            "slices": scan.slices if scan.slices is not None else min(w.B, 16),
-            "api": "simpletrain_b200.host_stream.HostScan.submit + wait (pinned host buffers, batch slices "
-                   "pipelined over copy-in / scan / copy-out streams, each step submitted before the "
-                   "previous step's results are awaited)"}
+            "ms_per_step": round(ms / steps, 4),
+            "copy_floor_ms_per_step": round(floor_ms, 4),
+            "frac_of_copy_floor": round(floor_ms / (ms / steps), 4),
+            "copy_floor": "each rank's h2d and d2h bytes moved at once (two streams, pinned memory) by all "
+                          "ranks together, max over ranks",
+            "api": "simpletrain_b200.host_stream.ShardedHostScan.submit + wait (pinned host pieces; copy-in / "
+                   "scan / copy-out streams; two buffer sets, each step submitted before the previous one's "
+                   "results are awaited)"}
+
+
+def copy_floor(h2d, d2h, dev, world, reps=5):
+    """Time moving h2d bytes host->device and d2h bytes device->host at once, on
+    every rank together: the link's floor under this run's conditions."""
+    import torch.distributed as dist
+    hi = torch.empty(h2d, dtype=torch.uint8, pin_memory=True)
+    di = torch.empty(h2d, dtype=torch.uint8, device=dev)
+    do = torch.empty(d2h, dtype=torch.uint8, device=dev)
+    ho = torch.empty(d2h, dtype=torch.uint8, pin_memory=True)
+    s1, s2 = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    best = None
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        a.record(cur)
+        s1.wait_stream(cur)
+        s2.wait_stream(cur)
+        with torch.cuda.stream(s1):
+            di.copy_(hi, non_blocking=True)
+        with torch.cuda.stream(s2):
+            ho.copy_(do, non_blocking=True)
+        cur.wait_stream(s1)
+        cur.wait_stream(s2)
+        b.record(cur)
+        torch.cuda.synchronize()
+        t = a.elapsed_time(b)
+        best = t if best is None else min(best, t)
+    return best
 
 
 # --------------------------------------------------------------------------- #
 # CPU legs (oracle port of the reference's torch path)
 # --------------------------------------------------------------------------- #
-def _cpu_sample_fn(w, n_heads, T):
-    """fwd(+bwd) of the oracle on n_heads (b, h) units of length T."""
+def _cpu_sample_fn(w, mode, n_heads, T):
+    """fwd(+bwd) of the oracle on n_heads (b, h) units of length T, in the
+    workload's semantics (literal K V^T with a float decay at D == chunk)."""
     from oracle.kda_oracle import chunk_scan
     from simpletrain_b200.workloads import custom
 
-    sub = w
-    ws = custom(1, n_heads, T, sub.D, dtype=sub.dtype, backward=sub.backward,
-                decay_mean=sub.decay_mean, s0_std=sub.s0_std)
+    ws = custom(1, n_heads, T, w.D, dtype=w.dtype, backward=w.backward,
+                decay_mean=w.decay_mean, s0_std=w.s0_std)
     inp = make_inputs(ws, seed=0)
+    literal = mode == 1
 
     def run():
-        leaves = [inp[n].float().requires_grad_(sub.backward) for n in ("q", "k", "v", "g")]
-        dl = inp["decay"].float().requires_grad_(sub.backward)
-        dec = dl.view(1, n_heads, sub.D, 1)
-        y, S = chunk_scan(*leaves, dec, sub.chunk,
-                          initial_state=inp["s0"], mode="corrected")
-        if sub.backward:
-            torch.autograd.grad([y], leaves + [dl], [inp["dy"].float()])
+        leaves = [inp[n].float().requires_grad_(w.backward) for n in ("q", "k", "v", "g")]
+        if literal:
+            dl = float(inp["decay"].mean())
+            wrt = leaves
+            dec = dl
+        else:
+            dl = inp["decay"].float().requires_grad_(w.backward)
+            wrt = leaves + [dl]
+            dec = dl.view(1, n_heads, w.D, 1)
+        y, S = chunk_scan(*leaves, dec, w.chunk, initial_state=inp["s0"],
+                          mode="literal" if literal else "corrected")
+        if w.backward:
+            torch.autograd.grad([y], wrt, [inp["dy"].float()])
     return run
 
 
-def cpu_baseline(w, budget_s=15.0, max_step_s=None):
+def cpu_baseline(w, mode, budget_s=15.0):
     """Time the oracle (a port of kernels/kda_kernel.py:244-297) on the host cores."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    heads = 1
-    T = w.T
-    fn = _cpu_sample_fn(w, heads, T)
+    heads, T = 1, w.T
+    fn = _cpu_sample_fn(w, mode, heads, T)
     fn()
     t0 = time.perf_counter()
     fn()
     per = time.perf_counter() - t0
-    if max_step_s is not None:
-        while per > max_step_s and T > w.chunk:
-            T = max(w.chunk, (T // 2) // w.chunk * w.chunk)
-            fn = _cpu_sample_fn(w, heads, T)
-            fn()
-            t0 = time.perf_counter()
-            fn()
-            per = time.perf_counter() - t0
-    else:
-        heads = int(max(1, min(w.B * w.H, (budget_s / 4) / max(per, 1e-6))))
-        fn = _cpu_sample_fn(w, heads, T)
-        fn()
+    heads = int(max(1, min(w.B * w.H, (budget_s / 4) / max(per, 1e-6))))
+    fn = _cpu_sample_fn(w, mode, heads, T)
+    fn()
     reps = 0
     t0 = time.perf_counter()
     while True:
@@ -412,27 +585,28 @@ def cpu_baseline(w, budget_s=15.0, max_step_s=None):
 def run_reference(args, w, rank, world):
     if rank != 0:
         return None
+    mode, _, _, sem_label = semantics(args, w)
     steps = args.steps if args.steps is not None else 10
     budget = 150.0
     step_budget = budget / max(1, steps + args.warmup)
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     heads, T = 1, w.T
-    fn = _cpu_sample_fn(w, heads, T)
+    fn = _cpu_sample_fn(w, mode, heads, T)
     fn()
     t0 = time.perf_counter()
     fn()
     per = time.perf_counter() - t0
     while per > step_budget and T > w.chunk:
         T = max(w.chunk, (T // 2) // w.chunk * w.chunk)
-        fn = _cpu_sample_fn(w, heads, T)
+        fn = _cpu_sample_fn(w, mode, heads, T)
         fn()
         t0 = time.perf_counter()
         fn()
         per = time.perf_counter() - t0
     if per * 2 < step_budget:
         heads = int(max(1, min(w.B * w.H, step_budget / max(per, 1e-6) * 0.8)))
-        fn = _cpu_sample_fn(w, heads, T)
+        fn = _cpu_sample_fn(w, mode, heads, T)
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
@@ -442,12 +616,14 @@ def run_reference(args, w, rank, world):
     value = heads * T * steps / el / w.H
     sample = (f"{heads} (batch,head) unit(s) x T={T}, D={w.D} per step, "
               f"{'fwd+bwd (autograd)' if w.backward else 'fwd'}, fp32 oracle port of "
-              f"kernels/kda_kernel.py:244-297 (K^T V update); tokens/s = token-heads/s / H")
+              f"kernels/kda_kernel.py:244-297 ({'literal K V^T' if mode == 1 else 'K^T V'} update); "
+              "tokens/s = token-heads/s / H")
+    strong = args.scaling == "strong"
     return {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(el / steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": dict(w.describe(), global_batch=w.B * world, seq_len=w.T),
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": config_dict(w, world, strong, sem_label, args),
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
@@ -553,15 +729,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="1b-fwdbwd", choices=sorted(WORKLOADS))
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: one problem sharded over the ranks (default); weak: a full batch per rank")
     ap.add_argument("--shape", default=None,
                     help="B,H,T,D: run a custom shape (profiling / sweeps) instead of --workload")
     ap.add_argument("--fwd-only", action="store_true", help="with --shape: forward pass only")
     ap.add_argument("--per-step", action="store_true",
                     help="per-token decay semantics (one decay per head) instead of chunk-constant decay")
+    ap.add_argument("--corrected", action="store_true",
+                    help="at D == chunk, the K^T V update instead of the reference's literal one")
+    ap.add_argument("--eager", action="store_true", help="launch each step eagerly instead of replaying a graph")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-slices", type=int, default=None,
-                    help="batch slices of the host-buffer pipeline (default min(B, 16))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--fused-ops", action="store_true",

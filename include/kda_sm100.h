@@ -147,6 +147,21 @@ int32_t kda_abi_version(void);
    (diagnostic; no counterpart in the reference). */
 uint64_t kda_launch_count(void);
 
+/* Per-kernel device times (diagnostic; no counterpart in the reference).
+   kda_trace_start(n): from now on each of the next n KDA kernel launches of
+   this library on the current device is bracketed by two CUDA events
+   recorded on its launching stream.  Returns KDA_OK, KDA_ERR_BAD_SHAPE for
+   n <= 0, or KDA_ERR_CUDA when the events cannot be created.
+   kda_trace_stop(ms, kernel, cap): stops recording, waits for the recorded
+   events and writes, in launch order, up to cap launch durations in
+   milliseconds and kernel ids (kda_kernel_name names them; -1 marks a launch
+   that failed).  Returns the number of launches recorded, or -KDA_ERR_CUDA.
+   One tracer per process: a second start discards the first; launches on
+   other devices and launches beyond n are not recorded. */
+int kda_trace_start(int32_t max_launches);
+int32_t kda_trace_stop(float *ms, int32_t *kernel, int32_t cap);
+const char *kda_kernel_name(int32_t kernel);
+
 /* Size of the fixed device scratch array used by kda_fwd_sm100_noalloc. */
 #define KDA_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 
@@ -159,7 +174,8 @@ uint64_t kda_launch_count(void);
    p->workspace_bytes are ignored); the scratch comes from a file-scope device
    array of KDA_NOALLOC_SCRATCH_BYTES that every GPU loading it holds until
    the process exits.
-   - Returns KDA_ERR_WORKSPACE, before enqueuing anything, when the problem
+   - Checks its arguments as kda_fwd_sm100 does (same status codes), then
+     returns KDA_ERR_WORKSPACE, before enqueuing anything, when the problem
      needs more than KDA_NOALLOC_SCRATCH_BYTES of scratch
      (kda_fwd_workspace_bytes() tells how much: 64 KiB per range boundary at
      D=128, 16 KiB at D=64, at most one boundary per resident CTA -- about
@@ -168,7 +184,10 @@ uint64_t kda_launch_count(void);
      plus a small header; only a KDA_SM100_RANGES override far above the CTA
      count reaches the limit).
    - The first call on a device looks up the array's device address; make that
-     first call before any stream capture.
+     first call before any stream capture.  A failed lookup returns
+     KDA_ERR_CUDA, leaves no CUDA error pending, and is retried by the next
+     call.  The address is kept for the life of the process: it is invalid
+     after cudaDeviceReset on that device.
    - Calls share the array and it keeps the last call's contents; each call
      clears what must start at zero on its own stream.  Calls that overlap on
      the GPU race on the array: serialise them (one stream, or events). */

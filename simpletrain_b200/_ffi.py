@@ -32,6 +32,7 @@ KDA_ERR_DEVICE_TIMEOUT = 64
 EXPORTED = (
     "kda_fwd_sm100", "kda_bwd_sm100", "kda_fwd_workspace_bytes", "kda_bwd_workspace_bytes",
     "kda_status_string", "kda_abi_version", "kda_launch_count", "kda_fwd_sm100_noalloc",
+    "kda_trace_start", "kda_trace_stop", "kda_kernel_name",
     # include/st_fused_ops.h
     "st_silu_mul_fwd", "st_silu_mul_bwd", "st_rmsnorm_residual_fwd", "st_rmsnorm_residual_bwd",
     "st_rmsnorm_residual_bwd_scratch", "st_cross_entropy_fwd", "st_cross_entropy_bwd",
@@ -100,6 +101,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.kda_launch_count.restype = ctypes.c_uint64
     lib.kda_fwd_sm100_noalloc.argtypes = [POINTER(KdaFwdParams), c_void_p]
     lib.kda_fwd_sm100_noalloc.restype = c_int32
+    lib.kda_trace_start.argtypes = [c_int32]
+    lib.kda_trace_start.restype = c_int32
+    lib.kda_trace_stop.argtypes = [POINTER(ctypes.c_float), POINTER(c_int32), c_int32]
+    lib.kda_trace_stop.restype = c_int32
+    lib.kda_kernel_name.argtypes = [c_int32]
+    lib.kda_kernel_name.restype = c_char_p
     ver = lib.kda_abi_version()
     if ver != ABI_VERSION:
         raise ImportError(f"KDA library ABI version {ver} != binding version {ABI_VERSION}; rebuild")
@@ -114,3 +121,45 @@ def status_string(code: int) -> str:
 def launch_count() -> int:
     """Kernels the library has launched in this process."""
     return int(load().kda_launch_count())
+
+
+class KernelTrace:
+    """CUDA-event device time of each KDA kernel launched inside the block.
+
+        with KernelTrace(max_launches=4096) as tr:
+            ...                                 # calls into the library
+        tr.launches                             # [(kernel name, ms), ...] in launch order
+        tr.per_kernel()                         # {name: (launches, mean ms)}
+
+    The events are recorded on each kernel's launching stream by the library
+    itself (``kda_trace_start`` / ``kda_trace_stop``), so every kernel of a
+    multi-kernel call (the backward's two passes) is timed on its own.
+    """
+
+    def __init__(self, max_launches: int = 4096):
+        self.max = int(max_launches)
+        self.launches = []
+
+    def __enter__(self):
+        rc = load().kda_trace_start(self.max)
+        if rc != KDA_OK:
+            raise RuntimeError(f"kda_trace_start: {status_string(rc)}")
+        return self
+
+    def __exit__(self, *exc):
+        lib = load()
+        ms = (ctypes.c_float * self.max)()
+        ids = (c_int32 * self.max)()
+        n = lib.kda_trace_stop(ms, ids, self.max)
+        if n < 0:
+            raise RuntimeError(f"kda_trace_stop: {status_string(-n)}")
+        n = min(n, self.max)
+        self.launches = [(lib.kda_kernel_name(ids[i]).decode(), float(ms[i])) for i in range(n) if ids[i] >= 0]
+        return False
+
+    def per_kernel(self):
+        out = {}
+        for name, t in self.launches:
+            c, s = out.get(name, (0, 0.0))
+            out[name] = (c + 1, s + t)
+        return {n: (c, s / c) for n, (c, s) in out.items()}

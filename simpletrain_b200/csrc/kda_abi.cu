@@ -9,15 +9,56 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "kda_internal.h"
 #include "kda_tc_epi.cuh"
 
 namespace {
 std::atomic<uint64_t> g_launches{0};
+
+// Launch tracer: a CUDA event pair around each traced launch, on its stream.
+struct Tracer {
+  std::mutex mu;
+  std::atomic<bool> on{false};
+  int dev = -1;
+  int used = 0;
+  std::vector<cudaEvent_t> ev;  // 2 per slot: before, after
+  std::vector<int> kernel;
+};
+Tracer g_trace;
+
+void trace_release() {
+  for (cudaEvent_t e : g_trace.ev) cudaEventDestroy(e);
+  g_trace.ev.clear();
+  g_trace.kernel.clear();
+  g_trace.used = 0;
+}
 }  // namespace
 
 void kda::count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int kda::trace_before(cudaStream_t st) {
+  if (!g_trace.on.load(std::memory_order_acquire)) return -1;
+  std::lock_guard<std::mutex> lock(g_trace.mu);
+  int dev = -1;
+  if (!g_trace.on.load(std::memory_order_relaxed) || cudaGetDevice(&dev) != cudaSuccess || dev != g_trace.dev ||
+      g_trace.used >= (int)g_trace.kernel.size())
+    return -1;
+  const int slot = g_trace.used++;
+  g_trace.kernel[slot] = -1;
+  cudaEventRecord(g_trace.ev[2 * slot], st);
+  return slot;
+}
+
+void kda::trace_after(int slot, int kernel, cudaStream_t st) {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lock(g_trace.mu);
+  if (slot >= (int)g_trace.kernel.size()) return;
+  g_trace.kernel[slot] = kernel;
+  cudaEventRecord(g_trace.ev[2 * slot + 1], st);
+}
 
 namespace {
 
@@ -183,6 +224,66 @@ int32_t kda_abi_version(void) { return KDA_ABI_VERSION; }
 
 uint64_t kda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int kda_trace_start(int32_t max_launches) {
+  if (max_launches <= 0) return KDA_ERR_BAD_SHAPE;
+  std::lock_guard<std::mutex> lock(g_trace.mu);
+  g_trace.on.store(false, std::memory_order_release);
+  trace_release();
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KDA_ERR_CUDA;
+  g_trace.ev.reserve(2 * (size_t)max_launches);
+  for (int i = 0; i < 2 * max_launches; ++i) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      trace_release();
+      cudaGetLastError();
+      return KDA_ERR_CUDA;
+    }
+    g_trace.ev.push_back(e);
+  }
+  g_trace.kernel.assign((size_t)max_launches, -1);
+  g_trace.dev = dev;
+  g_trace.on.store(true, std::memory_order_release);
+  return KDA_OK;
+}
+
+int32_t kda_trace_stop(float *ms, int32_t *kernel, int32_t cap) {
+  std::lock_guard<std::mutex> lock(g_trace.mu);
+  g_trace.on.store(false, std::memory_order_release);
+  const int n = g_trace.used;
+  int32_t rc = n;
+  for (int i = 0; i < n; ++i) {
+    if (i >= cap || ms == nullptr || kernel == nullptr) break;
+    float t = 0.f;
+    if (g_trace.kernel[i] < 0) {  // the launch itself failed: nothing to time
+      ms[i] = 0.f;
+      kernel[i] = -1;
+      continue;
+    }
+    if (cudaEventSynchronize(g_trace.ev[2 * i + 1]) != cudaSuccess ||
+        cudaEventElapsedTime(&t, g_trace.ev[2 * i], g_trace.ev[2 * i + 1]) != cudaSuccess) {
+      cudaGetLastError();
+      rc = -KDA_ERR_CUDA;
+      break;
+    }
+    ms[i] = t;
+    kernel[i] = g_trace.kernel[i];
+  }
+  trace_release();
+  return rc;
+}
+
+const char *kda_kernel_name(int32_t kernel) {
+  switch (kernel) {
+    case kda::kTraceFwd: return "fwd_tc_kernel";
+    case kda::kTraceBwdFwdDir: return "bwd_fwddir_tc_kernel";
+    case kda::kTraceBwdRevDir: return "bwd_revdir_tc_kernel";
+    case kda::kTraceAgg: return "agg_tc_kernel";
+    case kda::kTraceFold: return "entry_fold_kernel";
+    default: return "unknown";
+  }
+}
+
 const char *kda_status_string(int32_t s) {
   switch (s) {
     case KDA_OK: return "ok";
@@ -215,7 +316,11 @@ size_t kda_bwd_workspace_bytes(int32_t B, int32_t H, int32_t T, int32_t D, int32
          agg_bytes(B * H, nc, nr, 2 * carry_f4(D)) + agg_bytes(B * H, nc, nr, carry_f4(D));
 }
 
-int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
+}  // extern "C"
+
+// Every argument check of kda_fwd_sm100 except the workspace's (shared with
+// kda_fwd_sm100_noalloc, which checks its scratch size only after these).
+int kda::fwd_check_args(const kda_fwd_params *p) {
   if (p == nullptr) return KDA_ERR_NULL_ARGUMENT;
   int rc = check_common(p->B, p->H, p->T, p->D, p->chunk, p->dtype, p->flags);
   if (rc) return rc;
@@ -224,6 +329,19 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
   if ((rc = check_per_step(p->flags, p->dtype, p->decay, p->decay_stride_d, p->decay_scalar))) return rc;
   if ((p->state_in && !aligned16(p->state_in)) || (p->state_out && !aligned16(p->state_out)))
     return KDA_ERR_BAD_LAYOUT;
+  if (p->B == 0 || p->H == 0 || p->T == 0) return KDA_OK;  // no sequence is read or written
+  if ((rc = check_view(p->q, true)) || (rc = check_view(p->k, true)) || (rc = check_view(p->v, true)) ||
+      (rc = check_view(p->g, false)) || (rc = check_view(p->y, true)))
+    return rc;
+  return KDA_OK;
+}
+
+extern "C" {
+
+int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
+  int rc = kda::fwd_check_args(p);
+  if (rc) return rc;
+  const bool literal = (p->flags & KDA_FLAG_LITERAL) != 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->H == 0) return KDA_OK;  // nothing to read or write
   if (p->T == 0) {
@@ -236,9 +354,6 @@ int kda_fwd_sm100(const kda_fwd_params *p, kda_stream_t stream) {
     }
     return KDA_OK;
   }
-  if ((rc = check_view(p->q, true)) || (rc = check_view(p->k, true)) || (rc = check_view(p->v, true)) ||
-      (rc = check_view(p->g, false)) || (rc = check_view(p->y, true)))
-    return rc;
   const size_t need = kda_fwd_workspace_bytes(p->B, p->H, p->T, p->D, p->chunk, p->flags);
   if (need && (p->workspace == nullptr || p->workspace_bytes < need)) return KDA_ERR_WORKSPACE;
   kda::FwdArgs a{};

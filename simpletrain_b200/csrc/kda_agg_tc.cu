@@ -232,7 +232,9 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
   auto kern = agg_tc_kernel<T, D, LIT, PS, MODE, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   if (e != cudaSuccess) return e;
+  const int tr = trace_before(st);
   kern<<<q.nranges, kThreads + (agg_scales<PS, MODE>() ? 32 : 0), L::SMEM, st>>>(ma, mb, a, q);
+  trace_after(tr, kTraceAgg, st);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -328,7 +330,9 @@ __global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue q
 
 template <int D, bool REV, bool TAN>
 cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary, cudaStream_t st) {
+  const int tr = trace_before(st);
   entry_fold_kernel<D, REV, TAN><<<dim3(q.nranges, kFoldParts), kThreads, 0, st>>>(a, q, boundary);
+  trace_after(tr, kTraceFold, st);
   count_launches(1);
   return cudaGetLastError();
 }

@@ -958,7 +958,9 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q1.agg, q1.agg_f4, a.status};
     if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, a.s_in, st)) != cudaSuccess) return e;
   }
+  int tr = trace_before(st);
   k1<<<grid1, bwd_threads<PS>(), L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
+  trace_after(tr, kTraceBwdFwdDir, st);
   count_launches(1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -966,7 +968,9 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q2.agg, q2.agg_f4, a.status};
     if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, a.ds_out, st)) != cudaSuccess) return e;
   }
+  tr = trace_before(st);
   k2<<<grid2, bwd_threads<PS>(), L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
+  trace_after(tr, kTraceBwdRevDir, st);
   count_launches(1);
   return cudaGetLastError();
 }

@@ -496,7 +496,9 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
     e = launch_agg_tc(0, g, a.k, a.v, q, BF ? KDA_DTYPE_BF16 : KDA_DTYPE_F16, a.s_in, st);
     if (e != cudaSuccess) return e;
   }
+  const int tr = trace_before(st);
   kern<<<grid, fwd_threads<PS>(), L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
+  trace_after(tr, kTraceFwd, st);
   count_launches(1);
   return cudaGetLastError();
 }

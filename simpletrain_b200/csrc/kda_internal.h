@@ -65,6 +65,16 @@ __device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, in
 // Counts kernel launches for kda_launch_count().
 void count_launches(int n);
 
+// kda_fwd_sm100's argument checks, all but the workspace's: KDA_OK or a kda_status.
+int fwd_check_args(const kda_fwd_params *p);
+
+// Kernel ids of the launch tracer (kda_trace_start / kda_trace_stop).
+enum TraceKernel { kTraceFwd = 0, kTraceBwdFwdDir = 1, kTraceBwdRevDir = 2, kTraceAgg = 3, kTraceFold = 4 };
+// Bracket one kernel launch on `st`: trace_before returns a slot (or -1 when
+// the tracer is off or full), trace_after records the launch's end in it.
+int trace_before(cudaStream_t st);
+void trace_after(int slot, int kernel, cudaStream_t st);
+
 namespace tc {
 struct Queue;
 }

@@ -5,6 +5,7 @@ import os
 import re
 import shutil
 import subprocess
+import sys
 import tempfile
 
 import pytest
@@ -96,6 +97,52 @@ def _fwd_params(**kw):
 def test_forward_argument_checks(kw, code):
     lib = _ffi.load()
     assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params(**kw)), None) == code
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(D=96), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(chunk=32), _ffi.KDA_ERR_UNSUPPORTED),
+    (dict(T=-1), _ffi.KDA_ERR_BAD_SHAPE),
+    (dict(D=128, flags=_ffi.KDA_FLAG_LITERAL), _ffi.KDA_ERR_BAD_SHAPE),
+    (dict(), _ffi.KDA_ERR_NULL_ARGUMENT),
+    (dict(B=0), _ffi.KDA_OK),       # nothing to do: no scratch looked up, no pointers touched
+])
+def test_noalloc_checks_arguments_like_the_forward(kw, code):
+    lib = _ffi.load()
+    assert lib.kda_fwd_sm100_noalloc(ctypes.byref(_fwd_params(**kw)), None) == code
+    assert lib.kda_fwd_sm100(ctypes.byref(_fwd_params(**kw)), None) == code
+    assert lib.kda_fwd_sm100_noalloc(None, None) == _ffi.KDA_ERR_NULL_ARGUMENT
+
+
+_NOALLOC_ORDER_CHILD = r"""
+import ctypes
+from simpletrain_b200 import _ffi
+lib = _ffi.load()
+good = _ffi.KdaTensor(0x10000, 64 * 128, 64 * 128, 128, 1)
+p = _ffi.KdaFwdParams()
+p.B, p.H, p.T, p.D, p.chunk, p.dtype = 1, 600, 64, 128, 64, _ffi.KDA_DTYPE_BF16
+p.q = p.k = p.v = p.y = good
+need = lib.kda_fwd_workspace_bytes(1, 600, 64, 128, 64, 0)
+rc_big = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
+p.q = _ffi.KdaTensor(0x10008, 64 * 128, 64 * 128, 128, 1)      # misaligned, and still too big
+rc_bad = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
+print(need, rc_big, rc_bad, lib.kda_launch_count())
+"""
+
+
+def test_noalloc_reports_bad_arguments_before_its_size_limit():
+    """A problem over the scratch limit (forced with one work range per chunk)
+    is refused with KDA_ERR_WORKSPACE, but an argument error wins over it; nothing
+    is launched (the pointers are never touched)."""
+    env = dict(os.environ, KDA_SM100_RANGES="600")
+    out = subprocess.run([sys.executable, "-c", _NOALLOC_ORDER_CHILD], env=env, cwd=ROOT,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    need, rc_big, rc_bad, launched = (int(x) for x in out.stdout.split())
+    assert need > _ffi.NOALLOC_SCRATCH_BYTES
+    assert rc_big == _ffi.KDA_ERR_WORKSPACE
+    assert rc_bad == _ffi.KDA_ERR_BAD_LAYOUT
+    assert launched == 0
 
 
 def _bwd_params(**kw):

@@ -328,3 +328,24 @@ def test_layer_glue_after_the_scan_copies_nothing():
     t = o.transpose(1, 2)
     assert t.is_contiguous()
     assert t.contiguous().data_ptr() == o.data_ptr()
+
+
+def test_kernel_trace_times_each_kernel_of_a_step():
+    """The library's own CUDA-event tracer names and times every kernel launch."""
+    from simpletrain_b200._ffi import KernelTrace
+    inp = make_inputs(custom(4, 10, 1024, 128), seed=1, device=DEV)
+    q, k, v, g, dy = (inp[n] for n in ("q", "k", "v", "g", "dy"))
+    dec = inp["decay"].expand(4, 10, 128)
+    with torch.inference_mode(), KernelTrace(64) as tr:
+        for _ in range(3):
+            torch.ops.kda_b200.chunk_fwd(q, k, v, g, dec, 0.0, None, 64, 0, True)
+            torch.ops.kda_b200.chunk_bwd(q, k, v, g, dy, dec, 0.0, None, None, None, 64, 0, True, False)
+        torch.cuda.synchronize()
+    main = ("fwd_tc_kernel", "bwd_fwddir_tc_kernel", "bwd_revdir_tc_kernel")
+    names = [n for n, _ in tr.launches if n in main]
+    assert names == list(main) * 3
+    # 40 streams on 148 CTA slots are cut into ranges inside streams: the range
+    # aggregates and entry folds of the long-stream schedule run too
+    assert {n for n, _ in tr.launches} <= set(main) | {"agg_tc_kernel", "entry_fold_kernel"}
+    per = tr.per_kernel()
+    assert all(per[n][0] == 3 and 0.0 < per[n][1] < 100.0 for n in main)

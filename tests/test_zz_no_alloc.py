@@ -77,6 +77,21 @@ def test_noalloc_matches_allocating_entry_point_twice(B, H, T, D):
         assert max_rel(s.cpu(), s_ref.cpu()) <= TOL_STATE
 
 
+def test_default_schedules_fit_the_scratch():
+    """The scratch a forward needs is bounded by the device's CTA slots, not by
+    the problem: with the default schedule every shape fits the fixed array --
+    many short streams (one range per CTA slot, the D=64 kernels run two CTAs
+    per SM), a few long streams (range aggregates), each semantics."""
+    lib = _ffi.load()
+    shapes = [(64, 64, 64), (16, 10, 2048), (16, 8, 2048), (1, 1, 1 << 20), (1, 28, 32768), (3, 1, 64 * 1000)]
+    for D in (64, 128):
+        flag_sets = [0, _ffi.KDA_FLAG_PER_STEP] + ([_ffi.KDA_FLAG_LITERAL] if D == 64 else [])
+        for flags in flag_sets:
+            for B, H, T in shapes:
+                need = lib.kda_fwd_workspace_bytes(B, H, T, D, 64, flags)
+                assert need <= _ffi.NOALLOC_SCRATCH_BYTES, (B, H, T, D, flags, need)
+
+
 _OVERSIZE_CHILD = r"""
 import ctypes
 from simpletrain_b200 import _ffi
@@ -85,6 +100,8 @@ B, H, T, D = 1, 600, 64, 128          # 600 single-chunk streams, one range each
 need = lib.kda_fwd_workspace_bytes(B, H, T, D, 64, 0)
 p = _ffi.KdaFwdParams()
 p.B, p.H, p.T, p.D, p.chunk, p.dtype = B, H, T, D, 64, _ffi.KDA_DTYPE_BF16
+# well-formed views (never dereferenced: the size check refuses the call first)
+p.q = p.k = p.v = p.y = _ffi.KdaTensor(0x10000, T * D * H, T * D, D, 1)
 before = _ffi.launch_count()
 rc = lib.kda_fwd_sm100_noalloc(ctypes.byref(p), None)
 print(need, rc, _ffi.launch_count() - before)
