@@ -18,9 +18,11 @@ is split in time with one small all_gather of carried states per direction.
 Each rank's step is captured once in a CUDA graph and replayed (the step's
 launches cost more host time than a rank's share of the work takes on the
 device at 8 GPUs).  Per-kernel device times come from the library's own
-CUDA-event tracer (``kda_trace_start``) over an eager pass of the same steps
-right after the timed region.  At N > 1 the ranks' results are gathered on
-rank 0 after timing and checked against a single-GPU run of the whole problem.
+CUDA-event tracer (``kda_trace_start``): the step is captured once more with
+the tracer on, which brackets every kernel with event nodes of the graph, and
+replayed right after the timed region.  At N > 1 the ranks' results are
+gathered on rank 0 after timing and checked against a single-GPU run of the
+whole problem.
 
 Prints one JSON line (rank 0).
 """
@@ -282,14 +284,26 @@ def _run_ours(args, w, rank, world, local_rank, clk):
     ms = start.elapsed_time(end)
     graphed_launches = _ffi.launch_count() - launches0   # launches issued from the host (0 when replayed)
 
-    # ---- per-kernel device times: the library's event tracer, eager pass ----------
-    trace_steps = min(steps, 50)
+    # ---- per-kernel device times: the library's event tracer ----------------------
+    # (graph mode: the step captured once more with the tracer on, so each launch
+    # is bracketed by event nodes of the graph; the times are read after every replay)
+    trace_steps = min(steps, 50 if graph is None else 20)
     with torch.inference_mode():
         barrier()
         with _ffi.KernelTrace(max_launches=16 * trace_steps + 16) as tr:
-            for _ in range(trace_steps):
-                step()
-            torch.cuda.synchronize()
+            if graph is not None:
+                traced = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(traced):
+                    step()
+                for _ in range(trace_steps):
+                    traced.replay()
+                    torch.cuda.synchronize()
+                    tr.read()
+                del traced
+            else:
+                for _ in range(trace_steps):
+                    step()
+                torch.cuda.synchronize()
         barrier()
     per_kernel = tr.per_kernel()
     kernels_per_step = sum(c for c, _ in per_kernel.values()) / trace_steps
@@ -333,8 +347,10 @@ def _run_ours(args, w, rank, world, local_rank, clk):
                 "traffic": round(tph * rank_token_heads) if tph else None,
                 "algorithmic_bytes": dbytes, "peak_source": peaks["source"],
                 "kernel_ms": round(dms, 5),
-                "kernel_times": f"CUDA events around each launch (library tracer), eager pass of {trace_steps} steps "
-                                "right after the timed region",
+                "kernel_times": (f"CUDA events around each launch (library tracer), {trace_steps} "
+                                 + ("replays of the step captured as a CUDA graph with event nodes"
+                                    if graph is not None else "eager steps")
+                                 + " right after the timed region"),
                 "step_frac_hbm": round(step_bytes / per_step_s / 1e9 / peaks["hbm_gbs"], 4),
                 "step_frac_tensor": round(step_flops / per_step_s / 1e12 / peaks["bf16_tflops"], 4),
                 "step_bytes_per_rank": step_bytes}

@@ -157,8 +157,14 @@ uint64_t kda_launch_count(void);
    milliseconds and kernel ids (kda_kernel_name names them; -1 marks a launch
    that failed).  Returns the number of launches recorded, or -KDA_ERR_CUDA.
    One tracer per process: a second start discards the first; launches on
-   other devices and launches beyond n are not recorded. */
+   other devices and launches beyond n are not recorded.
+   A launch made while its stream is being captured into a CUDA graph gets
+   event-record nodes in the graph instead, recorded at every replay:
+   kda_trace_read (same arguments and result as kda_trace_stop, but it keeps
+   recording) then gives the times of the last replay.  Destroy such a graph
+   before kda_trace_stop, which frees the events. */
 int kda_trace_start(int32_t max_launches);
+int32_t kda_trace_read(float *ms, int32_t *kernel, int32_t cap);
 int32_t kda_trace_stop(float *ms, int32_t *kernel, int32_t cap);
 const char *kda_kernel_name(int32_t kernel);
 

@@ -32,7 +32,7 @@ KDA_ERR_DEVICE_TIMEOUT = 64
 EXPORTED = (
     "kda_fwd_sm100", "kda_bwd_sm100", "kda_fwd_workspace_bytes", "kda_bwd_workspace_bytes",
     "kda_status_string", "kda_abi_version", "kda_launch_count", "kda_fwd_sm100_noalloc",
-    "kda_trace_start", "kda_trace_stop", "kda_kernel_name",
+    "kda_trace_start", "kda_trace_read", "kda_trace_stop", "kda_kernel_name",
     # include/st_fused_ops.h
     "st_silu_mul_fwd", "st_silu_mul_bwd", "st_rmsnorm_residual_fwd", "st_rmsnorm_residual_bwd",
     "st_rmsnorm_residual_bwd_scratch", "st_cross_entropy_fwd", "st_cross_entropy_bwd",
@@ -103,8 +103,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.kda_fwd_sm100_noalloc.restype = c_int32
     lib.kda_trace_start.argtypes = [c_int32]
     lib.kda_trace_start.restype = c_int32
-    lib.kda_trace_stop.argtypes = [POINTER(ctypes.c_float), POINTER(c_int32), c_int32]
-    lib.kda_trace_stop.restype = c_int32
+    for fn in (lib.kda_trace_read, lib.kda_trace_stop):
+        fn.argtypes = [POINTER(ctypes.c_float), POINTER(c_int32), c_int32]
+        fn.restype = c_int32
     lib.kda_kernel_name.argtypes = [c_int32]
     lib.kda_kernel_name.restype = c_char_p
     ver = lib.kda_abi_version()
@@ -134,11 +135,33 @@ class KernelTrace:
     The events are recorded on each kernel's launching stream by the library
     itself (``kda_trace_start`` / ``kda_trace_stop``), so every kernel of a
     multi-kernel call (the backward's two passes) is timed on its own.
+
+    Launches captured into a CUDA graph inside the block are timed at every
+    replay: call ``read()`` after each replay has finished (it appends that
+    replay's launches), and destroy the graph before the block ends.
     """
 
     def __init__(self, max_launches: int = 4096):
         self.max = int(max_launches)
         self.launches = []
+        self._read = False
+
+    def _collect(self, fn):
+        lib = load()
+        ms = (ctypes.c_float * self.max)()
+        ids = (c_int32 * self.max)()
+        n = fn(ms, ids, self.max)
+        if n < 0:
+            raise RuntimeError(f"kernel trace: {status_string(-n)}")
+        n = min(n, self.max)
+        return [(lib.kda_kernel_name(ids[i]).decode(), float(ms[i])) for i in range(n) if ids[i] >= 0]
+
+    def read(self):
+        """Append the launches recorded so far (a graph's: those of its last replay)."""
+        self._read = True
+        got = self._collect(load().kda_trace_read)
+        self.launches += got
+        return got
 
     def __enter__(self):
         rc = load().kda_trace_start(self.max)
@@ -147,14 +170,9 @@ class KernelTrace:
         return self
 
     def __exit__(self, *exc):
-        lib = load()
-        ms = (ctypes.c_float * self.max)()
-        ids = (c_int32 * self.max)()
-        n = lib.kda_trace_stop(ms, ids, self.max)
-        if n < 0:
-            raise RuntimeError(f"kda_trace_stop: {status_string(-n)}")
-        n = min(n, self.max)
-        self.launches = [(lib.kda_kernel_name(ids[i]).decode(), float(ms[i])) for i in range(n) if ids[i] >= 0]
+        got = self._collect(load().kda_trace_stop)
+        if not self._read:
+            self.launches = got
         return False
 
     def per_kernel(self):

@@ -29,6 +29,38 @@ struct Tracer {
 };
 Tracer g_trace;
 
+// An event record on `st`: a plain record, or, while `st` is being captured
+// into a CUDA graph, an event-record node of the graph (recorded at every
+// replay).
+void trace_record(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, st);
+}
+
+// Elapsed times of the first min(used, cap) slots (the caller holds the lock).
+int32_t trace_collect(float *ms, int32_t *kernel, int32_t cap) {
+  const int n = g_trace.used;
+  for (int i = 0; i < n && i < cap && ms != nullptr && kernel != nullptr; ++i) {
+    float t = 0.f;
+    if (g_trace.kernel[i] < 0) {  // the launch itself failed: nothing to time
+      ms[i] = 0.f;
+      kernel[i] = -1;
+      continue;
+    }
+    if (cudaEventSynchronize(g_trace.ev[2 * i + 1]) != cudaSuccess ||
+        cudaEventElapsedTime(&t, g_trace.ev[2 * i], g_trace.ev[2 * i + 1]) != cudaSuccess) {
+      cudaGetLastError();
+      return -KDA_ERR_CUDA;
+    }
+    ms[i] = t;
+    kernel[i] = g_trace.kernel[i];
+  }
+  return n;
+}
+
 void trace_release() {
   for (cudaEvent_t e : g_trace.ev) cudaEventDestroy(e);
   g_trace.ev.clear();
@@ -48,7 +80,7 @@ int kda::trace_before(cudaStream_t st) {
     return -1;
   const int slot = g_trace.used++;
   g_trace.kernel[slot] = -1;
-  cudaEventRecord(g_trace.ev[2 * slot], st);
+  trace_record(g_trace.ev[2 * slot], st);
   return slot;
 }
 
@@ -57,7 +89,7 @@ void kda::trace_after(int slot, int kernel, cudaStream_t st) {
   std::lock_guard<std::mutex> lock(g_trace.mu);
   if (slot >= (int)g_trace.kernel.size()) return;
   g_trace.kernel[slot] = kernel;
-  cudaEventRecord(g_trace.ev[2 * slot + 1], st);
+  trace_record(g_trace.ev[2 * slot + 1], st);
 }
 
 namespace {
@@ -143,11 +175,30 @@ int ranges_override() {
 // backward: 128 streams of 32 chunks (D=128) 105 / 294 us cut, 68 / 226 us one
 // per stream; 96 streams 83 / 237 against 65 / 217; 64 streams of 64 chunks
 // 120 / 329 against 116 / 410, where cutting wins.
+//
+// Cut ranges hold at least KDA_SM100_MIN_CHUNKS chunks (default 4): a range's
+// fixed cost (setting up its pipeline, the fold of its entry carry, its share
+// of the decay gradient) is paid per range, so one short stream cut into one
+// range per CTA slot (a stream split in time between GPUs) runs faster on
+// fewer, longer ranges.
+int min_chunks_per_range() {
+  static const int v = [] {
+    const char *s = std::getenv("KDA_SM100_MIN_CHUNKS");
+    const int m = s ? std::atoi(s) : 4;
+    return m > 0 ? m : 1;
+  }();
+  return v;
+}
+
 int n_ranges(int nstreams, int nchunks, int slots) {
   const long long n = (long long)nstreams * nchunks;
-  int want = slots;
+  long long want = slots;
   if (ranges_override() > 0) want = ranges_override();
   else if (nstreams < slots && 2LL * nstreams >= slots) want = nstreams;
+  else if (nstreams < slots) {
+    const long long cap = (n + min_chunks_per_range() - 1) / min_chunks_per_range();
+    if (cap < want) want = cap > nstreams ? cap : nstreams;
+  }
   return (int)(n < want ? n : want);
 }
 
@@ -247,28 +298,15 @@ int kda_trace_start(int32_t max_launches) {
   return KDA_OK;
 }
 
+int32_t kda_trace_read(float *ms, int32_t *kernel, int32_t cap) {
+  std::lock_guard<std::mutex> lock(g_trace.mu);
+  return trace_collect(ms, kernel, cap);
+}
+
 int32_t kda_trace_stop(float *ms, int32_t *kernel, int32_t cap) {
   std::lock_guard<std::mutex> lock(g_trace.mu);
   g_trace.on.store(false, std::memory_order_release);
-  const int n = g_trace.used;
-  int32_t rc = n;
-  for (int i = 0; i < n; ++i) {
-    if (i >= cap || ms == nullptr || kernel == nullptr) break;
-    float t = 0.f;
-    if (g_trace.kernel[i] < 0) {  // the launch itself failed: nothing to time
-      ms[i] = 0.f;
-      kernel[i] = -1;
-      continue;
-    }
-    if (cudaEventSynchronize(g_trace.ev[2 * i + 1]) != cudaSuccess ||
-        cudaEventElapsedTime(&t, g_trace.ev[2 * i], g_trace.ev[2 * i + 1]) != cudaSuccess) {
-      cudaGetLastError();
-      rc = -KDA_ERR_CUDA;
-      break;
-    }
-    ms[i] = t;
-    kernel[i] = g_trace.kernel[i];
-  }
+  const int32_t rc = trace_collect(ms, kernel, cap);
   trace_release();
   return rc;
 }

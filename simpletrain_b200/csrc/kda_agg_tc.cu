@@ -239,99 +239,110 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
   return cudaGetLastError();
 }
 
-// Entry carries of long streams, after the aggregates: for every range whose
-// first piece (reverse: last piece) continues a stream begun in another range,
-// the stream's boundary carry x (initial state; reverse: final-state gradient;
-// `boundary`, or zero) is folded through the aggregates of the publishing pieces
-// of the ranges in between, in stream order,
+// Entry carries of long streams, after the aggregates.  One group of CTAs per
+// stream that spans several ranges walks the ranges it spans once, in stream
+// order (reverse: from the stream's end), folding the boundary carry x (initial
+// state; reverse: final-state gradient; `boundary`, or zero) through the
+// aggregate of each range's publishing piece,
 //   x <- A_j x + x_loc_j    (with the tangent: t <- A_j t + 64 n_j A_j x + t_loc_j),
-// A_j the product of piece j's chunk decays, and goes to the range's boundary
-// slot, where the main kernel reads it without waiting.  The epilogue thread
-// layout of the main kernels (slot = each thread's carry registers in order);
-// grid (ranges, kFoldParts): each CTA folds one slice of every thread's carry,
-// so a thread holds its slice of an aggregate in one batch of loads and pays
-// one memory round trip per range it folds.
-constexpr int kFoldParts = 4;
+// A_j the product of piece j's chunk decays, and stores the carry entering the
+// next range into that range boundary's slot, where the main kernel reads it
+// without waiting.  Slots and aggregates follow the epilogue thread layout of
+// the main kernels (a thread's carry registers in order); grid (streams,
+// fold_parts): each CTA carries one float4 of every thread's carry, so the
+// aggregates of many links are loaded ahead of the multiply-adds that use them
+// and a link costs little more than its arithmetic.  The fold order is fixed,
+// so the result does not depend on timing.
+template <int D>
+constexpr int fold_parts() { return Carry<D>::FLOATS / 4; }
+constexpr int kLinkBatch = 8;        // links whose aggregates are loaded together
+constexpr int kMaxFoldLinks = 1024;  // links whose chunk counts are staged in shared memory
 
 template <int D, bool REV, bool TAN>
 __global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
   if (threadIdx.x < 64) return;
-  const Span sp = span_of(qu, (int)blockIdx.x, false);
-  int stream;
-  if (!REV) {
-    if (sp.c0 == 0) return;  // starts its stream: nothing to fold
-    stream = sp.s0;
-  } else {
-    if (sp.c1 == qu.nchunks) return;
-    stream = sp.s1;
-  }
-  constexpr int NR = Carry<D>::NR, NV = Carry<D>::NV, N4 = Carry<D>::FLOATS / 4, NP = N4 / kFoldParts;
-  static_assert(N4 % kFoldParts == 0, "carry slices");
+  const int stream = (int)blockIdx.x;
+  const long long first = (long long)stream * qu.nchunks;
+  const int j_lo = range_of(qu, first), j_hi = range_of(qu, first + qu.nchunks - 1);
+  if (j_lo == j_hi) return;  // the stream lies in one range: no carry crosses a boundary
+  constexpr int NV = Carry<D>::NV, N4 = Carry<D>::FLOATS / 4;
+  static_assert(N4 == fold_parts<D>(), "one float4 per CTA");
   const Epi e;
-  Carry<D> rows;  // row and column indices of this thread's carry registers only
-  rows.init_rows(e);
-  const int i0 = (int)blockIdx.y * NP;
-  // boundary carry, float4 i4 of this thread's registers = row-major columns col(i)..col(i)+3
-  float4 xs[NP], ts[NP];
-  for (int k = 0; k < NP; ++k) {
-    const int i4 = i0 + k, r = (4 * i4) / NV, c = (4 * i4) % NV;
-    xs[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    ts[k] = xs[k];
-    if (boundary) {
-      const float *src = boundary + (size_t)stream * D * D + (size_t)rows.row[r] * D;
-      const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + rows.col(e, c)));
-      const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + rows.col(e, c + 2)));
-      xs[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
-    }
+  const int i4 = (int)blockIdx.y;
+  const int row = Carry<D>::row_of(e, (4 * i4) / NV), col = (4 * i4) % NV;
+  float4 x = make_float4(0.f, 0.f, 0.f, 0.f), t = x;
+  if (boundary) {
+    const float *src = boundary + (size_t)stream * D * D + (size_t)row * D;
+    const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, col)));
+    const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, col + 2)));
+    x = make_float4(lo.x, lo.y, hi.x, hi.y);
   }
   const int b = stream / a.H, h = stream - b * a.H;
   const int Ltail = a.T - (qu.nchunks - 1) * 64;
-  float af[NR], at[NR];
-  for (int r = 0; r < NR; ++r) {
-    af[r] = chunk_alpha(a.decay, b, h, rows.row[r], 64, 64);
-    at[r] = chunk_alpha(a.decay, b, h, rows.row[r], Ltail, 64);
-  }
-  const long long edge = (long long)stream * qu.nchunks + (REV ? qu.nchunks - 1 : 0);
-  for (int j = range_of(qu, edge); j != sp.r; j += REV ? -1 : 1) {
+  const float af = chunk_alpha(a.decay, b, h, row, 64, 64), at = chunk_alpha(a.decay, b, h, row, Ltail, 64);
+
+  // links in fold order: the range, and its piece's chunk count (negative: the
+  // piece holds the stream's ragged last chunk), staged once by all threads --
+  // a range's boundaries take 64-bit divisions
+  const int nlinks = j_hi - j_lo;
+  auto link_range = [&](int l) { return REV ? j_hi - l : j_lo + l; };
+  auto link_chunks = [&](int l) {
     int s, cb, ce;
-    published_piece(qu, span_of(qu, j, false), REV, s, cb, ce);
-    const int n = ce - cb;
-    const bool tail = REV && ce == qu.nchunks;
-    const float4 *ag = agg_ptr(qu, j);
-    float4 g[NP], gt[NP];
-#pragma unroll
-    for (int k = 0; k < NP; ++k) {
-      g[k] = __ldcg(ag + (i0 + k) * kEpi + e.et);
-      if constexpr (TAN) gt[k] = __ldcg(ag + (N4 + i0 + k) * kEpi + e.et);
-    }
-    float A[NR], An[NR];
-    for (int r = 0; r < NR; ++r) {
-      A[r] = tail ? powf(af[r], (float)(n - 1)) * at[r] : powf(af[r], (float)n);
-      An[r] = 64.f * (float)n * A[r];
-    }
-#pragma unroll
-    for (int k = 0; k < NP; ++k) {
-      const int r = (4 * (i0 + k)) / NV;
-      if constexpr (TAN)
-        ts[k] = make_float4(fmaf(A[r], ts[k].x, fmaf(An[r], xs[k].x, gt[k].x)),
-                            fmaf(A[r], ts[k].y, fmaf(An[r], xs[k].y, gt[k].y)),
-                            fmaf(A[r], ts[k].z, fmaf(An[r], xs[k].z, gt[k].z)),
-                            fmaf(A[r], ts[k].w, fmaf(An[r], xs[k].w, gt[k].w)));
-      xs[k] = make_float4(fmaf(A[r], xs[k].x, g[k].x), fmaf(A[r], xs[k].y, g[k].y), fmaf(A[r], xs[k].z, g[k].z),
-                          fmaf(A[r], xs[k].w, g[k].w));
-    }
+    published_piece(qu, span_of(qu, link_range(l), false), REV, s, cb, ce);
+    return (REV && ce == qu.nchunks) ? -(ce - cb) : ce - cb;
+  };
+  __shared__ int link_n[kMaxFoldLinks];
+  const bool staged = nlinks <= kMaxFoldLinks;
+  if (staged) {
+    for (int l = e.et; l < nlinks; l += kEpi) link_n[l] = link_chunks(l);
+    named_bar_sync(1, kEpi);
   }
-  float4 *slot = slot_ptr(qu, REV ? sp.r + 1 : sp.r);
-  for (int k = 0; k < NP; ++k) {
-    __stcg(slot + (i0 + k) * kEpi + e.et, xs[k]);
-    if constexpr (TAN) __stcg(slot + (N4 + i0 + k) * kEpi + e.et, ts[k]);
+
+  int n_prev = 0;
+  bool tail_prev = false;
+  float A = 1.f;
+  for (int base = 0; base < nlinks; base += kLinkBatch) {
+    float4 g[kLinkBatch], gt[TAN ? kLinkBatch : 1];
+#pragma unroll
+    for (int u = 0; u < kLinkBatch; ++u) {
+      if (base + u < nlinks) {
+        const float4 *ag = agg_ptr(qu, link_range(base + u));
+        g[u] = __ldcg(ag + i4 * kEpi + e.et);
+        if constexpr (TAN) gt[u] = __ldcg(ag + (N4 + i4) * kEpi + e.et);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kLinkBatch; ++u) {
+      const int l = base + u;
+      if (l >= nlinks) break;
+      const int cn = staged ? link_n[l] : link_chunks(l);
+      const int n = cn < 0 ? -cn : cn;
+      const bool tail = cn < 0;
+      if (n != n_prev || tail != tail_prev) {
+        A = tail ? powf(af, (float)(n - 1)) * at : powf(af, (float)n);
+        n_prev = n;
+        tail_prev = tail;
+      }
+      if constexpr (TAN) {
+        const float An = 64.f * (float)n * A;
+        t = make_float4(fmaf(A, t.x, fmaf(An, x.x, gt[u].x)), fmaf(A, t.y, fmaf(An, x.y, gt[u].y)),
+                        fmaf(A, t.z, fmaf(An, x.z, gt[u].z)), fmaf(A, t.w, fmaf(An, x.w, gt[u].w)));
+      }
+      x = make_float4(fmaf(A, x.x, g[u].x), fmaf(A, x.y, g[u].y), fmaf(A, x.z, g[u].z), fmaf(A, x.w, g[u].w));
+      // the carry entering the next range in fold order: its boundary slot
+      // (forward: range j + 1's entry, slot j + 1; reverse: range j - 1's, slot j)
+      const int j = link_range(l);
+      float4 *slot = slot_ptr(qu, REV ? j : j + 1);
+      __stcg(slot + i4 * kEpi + e.et, x);
+      if constexpr (TAN) __stcg(slot + (N4 + i4) * kEpi + e.et, t);
+    }
   }
 }
 
 template <int D, bool REV, bool TAN>
 cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary, cudaStream_t st) {
   const int tr = trace_before(st);
-  entry_fold_kernel<D, REV, TAN><<<dim3(q.nranges, kFoldParts), kThreads, 0, st>>>(a, q, boundary);
+  entry_fold_kernel<D, REV, TAN><<<dim3(q.nstreams, fold_parts<D>()), kThreads, 0, st>>>(a, q, boundary);
   trace_after(tr, kTraceFold, st);
   count_launches(1);
   return cudaGetLastError();

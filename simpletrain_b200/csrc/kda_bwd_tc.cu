@@ -426,9 +426,14 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           for (int r = 0; r < Carry<D>::NR; ++r) alr[r] = (Lc == 64) ? af[r] : at[r];
           const float Lf = (float)Lc;
           // factors of the loaded carry for the operand and for tensor memory; per-step:
-          // both a^kRef S_{c-1} (S_{c-1} = a^(64-kRef) Z from tensor memory past the first chunk)
-          float sop = 1.f, stm = alr[0];
-          if constexpr (PS) sop = stm = (c == u.c_begin) ? am : af[0];
+          // both a^kRef S_{c-1}.  Past the first chunk tensor memory holds
+          // Z = a^(kRef-64) S_{c-1}, brought back to S_{c-1} by a^(64-kRef) first: the
+          // single factor a^64 would flush to zero in fp32 for a < 2^(-126/64) ~ 0.26
+          float sop = 1.f, stm = alr[0], pre = 1.f;
+          if constexpr (PS) {
+            sop = stm = am;
+            if (c != u.c_begin) pre = au_f;
+          }
           if (D == 128) {
             const int row = Td.row[0];
             constexpr int W = Carry<D>::W;
@@ -474,6 +479,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                     tmem_ld_32x32b_x32(tz, u32);
                   }
                 }
+                if constexpr (PS)
+                  for (int k = 0; k < SW; ++k) u32[k] = __float_as_uint(pre * __uint_as_float(u32[k]));
                 if (want_dd) {
                   float acc = 0.f;
                   for (int k = 0; k < SW; ++k) acc = fmaf(Td.x[0][SW * sl + k], __uint_as_float(w32[k]), acc);
@@ -506,6 +513,9 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
               else Sp.load_rm(e, a.s_in ? a.s_in + sbase : nullptr);
             } else {
               Sp.tmem_load(e, tmem, L::A_Z);
+              if constexpr (PS)
+                for (int r = 0; r < Carry<D>::NR; ++r)
+                  for (int k = 0; k < Carry<D>::NV; ++k) Sp.x[r][k] *= pre;
             }
             if (want_dd) {
               Carry<D> W;
@@ -564,12 +574,19 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       // piece end: the last K^T V has landed in tensor memory
       if (!mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag)) break;
       tc_fence_after();
-      if (want_dd && prev) {
-        // the previous range's share of the decay gradient (that range runs in parallel)
-        if (!chain_wait(e, qu, u.wait_slot, a.status, abort_flag, 2)) break;
-        const float4 v = __ldcg(prev + 2 * CF4 * kEpi + e.et);
-        dl[0] += v.x;
-        if (Carry<D>::NR > 1) dl[Carry<D>::NR - 1] += v.y;
+      if (want_dd && prev && u.pub_slot < 0) {
+        // the piece that ends a stream begun in earlier ranges adds their shares of
+        // the decay gradient (each range publishes only its own, at level 2): all
+        // flags are waited for at once, then the shares are summed in stream order,
+        // so the sum is the same whichever range finished first
+        const int j0 = range_of(qu, (long long)u.stream * qu.nchunks);
+        if (!shares_wait(e, qu, j0 + 1, u.range + 1, a.status, abort_flag)) break;
+#pragma unroll 4
+        for (int j = j0; j < u.range; ++j) {
+          const float4 v = __ldcg(slot_ptr(qu, j + 1) + 2 * CF4 * kEpi + e.et);
+          dl[0] += v.x;
+          if (Carry<D>::NR > 1) dl[Carry<D>::NR - 1] += v.y;
+        }
       }
       if (u.pub_slot >= 0) {
         float4 *slot = slot_ptr(qu, u.pub_slot);

@@ -120,12 +120,17 @@ struct Carry {
   static constexpr int FLOATS = NR * NV;  // per thread
   float x[NR][NV];
   int row[NR];
-  __device__ __forceinline__ int col(const Epi &e, int i) const {
+  // carry layout: register column i of a thread is matrix column col_of(e, i);
+  // its register row r is matrix row row_of(e, r)
+  static __device__ __forceinline__ int col_of(const Epi &e, int i) {
     return (D == 128) ? W * e.cg + i : W * e.cg + 8 * (i >> 1) + e.cq + (i & 1);
   }
+  static __device__ __forceinline__ int row_of(const Epi &e, int r) {
+    return (D == 128) ? 32 * e.sp + e.lane : e.r0 + 8 * r;
+  }
+  __device__ __forceinline__ int col(const Epi &e, int i) const { return col_of(e, i); }
   __device__ void init_rows(const Epi &e) {
-    if (D == 128) row[0] = 32 * e.sp + e.lane;
-    else { row[0] = e.r0; row[NR - 1] = e.r0 + 8; }
+    for (int r = 0; r < NR; ++r) row[r] = row_of(e, r);
   }
   __device__ void zero() {
     for (int r = 0; r < NR; ++r)
@@ -529,6 +534,31 @@ __device__ __forceinline__ bool chain_wait(const Epi &e, const Queue &qu, int sl
   }
   named_bar_sync(1, kEpi);
   return ok_flag != 0;
+}
+
+// Epilogue: wait until every boundary slot in [lo, hi) has been published to
+// `level`, the slots spread over the epilogue threads so that the waits overlap
+// (each bounded), then barrier.  Returns false on timeout.
+__device__ __forceinline__ bool shares_wait(const Epi &e, const Queue &qu, int lo, int hi, int32_t *status,
+                                            volatile int *abort_flag, int level = 2) {
+  __shared__ int all_ok;
+  if (e.et == 0) all_ok = 1;
+  named_bar_sync(1, kEpi);
+  for (int s = lo + e.et; s < hi; s += kEpi) {
+    if (ld_acquire(qu.flags + s) >= level) continue;
+    const long long t0 = clock64();
+    while (ld_acquire(qu.flags + s) < level) {
+      if (*abort_flag || clock64() - t0 > kWaitCycles) {
+        if (status) atomicOr(status, KDA_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+        all_ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  named_bar_sync(1, kEpi);
+  return all_ok != 0;
 }
 
 // Epilogue: after every thread stored its part of the slot, publish it.  The

@@ -194,10 +194,14 @@ def test_layout_rules_are_enforced_before_any_launch():
 
 def test_workspace_sizes_and_status_strings():
     lib = _ffi.load()
-    # one fp32 state handoff slot per boundary between work ranges; 12 chunks here,
-    # so (without a GPU or on a big one) one range per chunk: 13 boundaries
-    assert lib.kda_fwd_workspace_bytes(2, 3, 128, 128, 64, 0) >= 13 * 128 * 128 * 4
-    assert lib.kda_bwd_workspace_bytes(2, 3, 128, 128, 64, 0) >= 13 * 3 * 128 * 128 * 4
+    # one fp32 state handoff slot per boundary between work ranges; 6 streams of 2
+    # chunks here: cut ranges hold at least 4 chunks, so one range per stream, 7 boundaries
+    assert lib.kda_fwd_workspace_bytes(2, 3, 128, 128, 64, 0) >= 7 * 128 * 128 * 4
+    assert lib.kda_bwd_workspace_bytes(2, 3, 128, 128, 64, 0) >= 7 * 3 * 128 * 128 * 4
+    # one stream of 256 chunks: 64 ranges of 4 chunks (not one per CTA slot), each with
+    # a boundary slot and a range aggregate of 64 KiB
+    slot = 128 * 128 * 4
+    assert 129 * slot <= lib.kda_fwd_workspace_bytes(1, 1, 256 * 64, 128, 64, 0) < 130 * slot
     # bounded by the CTA count, not by the problem size
     assert lib.kda_fwd_workspace_bytes(64, 64, 1 << 16, 128, 64, 0) < 64 << 20
     assert lib.kda_fwd_workspace_bytes(0, 3, 128, 128, 64, 0) < 1024

@@ -129,6 +129,7 @@ SMALL = [
     (2, 2, 130, 64, False, "0.5", True),
     (1, 1, 1, 64, True, "0.97", True),
     (1, 2, 77, 128, False, "0.125", True),     # the smallest decay the row scaling takes
+    (1, 2, 200, 64, True, "0.2", True),        # a^64 below fp32's range, four chunks carried in one range
     (1, 2, 192, 128, True, "1.0", False),      # no decay: plain causal linear attention
 ]
 

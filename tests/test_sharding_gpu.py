@@ -126,3 +126,41 @@ def test_forward_and_backward_replay_in_a_cuda_graph():
         torch.cuda.synchronize()
     for a, b in zip(out, eager):
         assert torch.equal(a, b)
+
+
+def test_kernel_trace_inside_a_cuda_graph():
+    """The tracer brackets captured launches with event nodes: after each replay
+    it reads that replay's per-kernel device times."""
+    from simpletrain_b200._ffi import KernelTrace
+    B, H, T, D = 4, 10, 1024, 128
+    inp = make_inputs(custom(B, H, T, D), seed=2, device=DEV)
+    q, k, v, g, dy = (inp[n] for n in ("q", "k", "v", "g", "dy"))
+    dec = inp["decay"].expand(B, H, D)
+
+    def step():
+        torch.ops.kda_b200.chunk_fwd(q, k, v, g, dec, 0.0, None, 64, 0, True)
+        torch.ops.kda_b200.chunk_bwd(q, k, v, g, dy, dec, 0.0, None, None, None, 64, 0, True, False)
+
+    with torch.inference_mode():
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with KernelTrace(64) as tr:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            per_replay = []
+            for _ in range(3):
+                graph.replay()
+                torch.cuda.synchronize()
+                per_replay.append(tr.read())
+            del graph
+    main = ("fwd_tc_kernel", "bwd_fwddir_tc_kernel", "bwd_revdir_tc_kernel")
+    for got in per_replay:
+        names = [n for n, _ in got if n in main]
+        assert names == list(main)
+        assert all(0.0 < ms < 100.0 for _, ms in got)
+    assert len(tr.launches) == sum(len(r) for r in per_replay)
