@@ -248,34 +248,37 @@ cudaError_t agg_launch(const AggArgs &a, const View &va, const View &vb, const Q
 // A_j the product of piece j's chunk decays, and stores the carry entering the
 // next range into that range boundary's slot, where the main kernel reads it
 // without waiting.  Slots and aggregates follow the epilogue thread layout of
-// the main kernels (a thread's carry registers in order); grid (streams,
-// fold_parts): each CTA carries one float4 of every thread's carry, so the
-// aggregates of many links are loaded ahead of the multiply-adds that use them
-// and a link costs little more than its arithmetic.  The fold order is fixed,
-// so the result does not depend on timing.
-template <int D>
-constexpr int fold_parts() { return Carry<D>::FLOATS / 4; }
-constexpr int kLinkBatch = 8;        // links whose aggregates are loaded together
+// the main kernels (a thread's carry registers in order); a CTA is that layout's
+// 256 threads without the main kernels' producer warps, and grid (streams,
+// parts) splits every thread's carry into parts of NP float4, NP chosen so the
+// grid fits one wave: the aggregates of several links are loaded ahead of the
+// multiply-adds that use them.  The fold order is fixed, so the result does not
+// depend on timing.
 constexpr int kMaxFoldLinks = 1024;  // links whose chunk counts are staged in shared memory
 
-template <int D, bool REV, bool TAN>
-__global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
-  if (threadIdx.x < 64) return;
+template <int D, bool REV, bool TAN, int NP>
+__global__ void __launch_bounds__(kEpi) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
   const int stream = (int)blockIdx.x;
   const long long first = (long long)stream * qu.nchunks;
   const int j_lo = range_of(qu, first), j_hi = range_of(qu, first + qu.nchunks - 1);
   if (j_lo == j_hi) return;  // the stream lies in one range: no carry crosses a boundary
   constexpr int NV = Carry<D>::NV, N4 = Carry<D>::FLOATS / 4;
-  static_assert(N4 == fold_parts<D>(), "one float4 per CTA");
-  const Epi e;
-  const int i4 = (int)blockIdx.y;
-  const int row = Carry<D>::row_of(e, (4 * i4) / NV), col = (4 * i4) % NV;
-  float4 x = make_float4(0.f, 0.f, 0.f, 0.f), t = x;
-  if (boundary) {
-    const float *src = boundary + (size_t)stream * D * D + (size_t)row * D;
-    const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, col)));
-    const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, col + 2)));
-    x = make_float4(lo.x, lo.y, hi.x, hi.y);
+  static_assert(N4 % NP == 0 && NV % (4 * NP) == 0, "a part lies in one carry row");
+  constexpr int U = (TAN ? 4 : 8) / NP > 0 ? (TAN ? 4 : 8) / NP : 1;  // links per batch of loads
+  const Epi e(64 + (int)threadIdx.x);
+  const int i0 = (int)blockIdx.y * NP;
+  const int row = Carry<D>::row_of(e, (4 * i0) / NV);
+  float4 x[NP], t[NP];
+  for (int k = 0; k < NP; ++k) {
+    x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    t[k] = x[k];
+    if (boundary) {
+      const int c = (4 * (i0 + k)) % NV;
+      const float *src = boundary + (size_t)stream * D * D + (size_t)row * D;
+      const float2 lo = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, c)));
+      const float2 hi = __ldg(reinterpret_cast<const float2 *>(src + Carry<D>::col_of(e, c + 2)));
+      x[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
   }
   const int b = stream / a.H, h = stream - b * a.H;
   const int Ltail = a.T - (qu.nchunks - 1) * 64;
@@ -295,24 +298,27 @@ __global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue q
   const bool staged = nlinks <= kMaxFoldLinks;
   if (staged) {
     for (int l = e.et; l < nlinks; l += kEpi) link_n[l] = link_chunks(l);
-    named_bar_sync(1, kEpi);
+    __syncthreads();
   }
 
   int n_prev = 0;
   bool tail_prev = false;
   float A = 1.f;
-  for (int base = 0; base < nlinks; base += kLinkBatch) {
-    float4 g[kLinkBatch], gt[TAN ? kLinkBatch : 1];
+  for (int base = 0; base < nlinks; base += U) {
+    float4 g[U][NP], gt[U][TAN ? NP : 1];
 #pragma unroll
-    for (int u = 0; u < kLinkBatch; ++u) {
+    for (int u = 0; u < U; ++u) {
       if (base + u < nlinks) {
         const float4 *ag = agg_ptr(qu, link_range(base + u));
-        g[u] = __ldcg(ag + i4 * kEpi + e.et);
-        if constexpr (TAN) gt[u] = __ldcg(ag + (N4 + i4) * kEpi + e.et);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          g[u][k] = __ldcg(ag + (i0 + k) * kEpi + e.et);
+          if constexpr (TAN) gt[u][k] = __ldcg(ag + (N4 + i0 + k) * kEpi + e.et);
+        }
       }
     }
 #pragma unroll
-    for (int u = 0; u < kLinkBatch; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int l = base + u;
       if (l >= nlinks) break;
       const int cn = staged ? link_n[l] : link_chunks(l);
@@ -323,26 +329,42 @@ __global__ void __launch_bounds__(kThreads) entry_fold_kernel(AggArgs a, Queue q
         n_prev = n;
         tail_prev = tail;
       }
-      if constexpr (TAN) {
-        const float An = 64.f * (float)n * A;
-        t = make_float4(fmaf(A, t.x, fmaf(An, x.x, gt[u].x)), fmaf(A, t.y, fmaf(An, x.y, gt[u].y)),
-                        fmaf(A, t.z, fmaf(An, x.z, gt[u].z)), fmaf(A, t.w, fmaf(An, x.w, gt[u].w)));
-      }
-      x = make_float4(fmaf(A, x.x, g[u].x), fmaf(A, x.y, g[u].y), fmaf(A, x.z, g[u].z), fmaf(A, x.w, g[u].w));
       // the carry entering the next range in fold order: its boundary slot
       // (forward: range j + 1's entry, slot j + 1; reverse: range j - 1's, slot j)
       const int j = link_range(l);
       float4 *slot = slot_ptr(qu, REV ? j : j + 1);
-      __stcg(slot + i4 * kEpi + e.et, x);
-      if constexpr (TAN) __stcg(slot + (N4 + i4) * kEpi + e.et, t);
+#pragma unroll
+      for (int k = 0; k < NP; ++k) {
+        if constexpr (TAN) {
+          const float An = 64.f * (float)n * A;
+          t[k] = make_float4(fmaf(A, t[k].x, fmaf(An, x[k].x, gt[u][k].x)),
+                             fmaf(A, t[k].y, fmaf(An, x[k].y, gt[u][k].y)),
+                             fmaf(A, t[k].z, fmaf(An, x[k].z, gt[u][k].z)),
+                             fmaf(A, t[k].w, fmaf(An, x[k].w, gt[u][k].w)));
+        }
+        x[k] = make_float4(fmaf(A, x[k].x, g[u][k].x), fmaf(A, x[k].y, g[u][k].y), fmaf(A, x[k].z, g[u][k].z),
+                           fmaf(A, x[k].w, g[u][k].w));
+        __stcg(slot + (i0 + k) * kEpi + e.et, x[k]);
+        if constexpr (TAN) __stcg(slot + (N4 + i0 + k) * kEpi + e.et, t[k]);
+      }
     }
   }
 }
 
 template <int D, bool REV, bool TAN>
 cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary, cudaStream_t st) {
+  // float4 per thread per CTA: as few as fit one wave of two 256-thread CTAs per SM
+  // (a part lies in one carry row: at most 4 float4 at D=128, 2 at D=64)
+  constexpr int N4 = Carry<D>::FLOATS / 4, NP_MAX = Carry<D>::NV / 4 < 4 ? Carry<D>::NV / 4 : 4;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int np = 1;
+  while (np < NP_MAX && (long long)q.nstreams * (N4 / np) > 2LL * sms) np *= 2;
   const int tr = trace_before(st);
-  entry_fold_kernel<D, REV, TAN><<<dim3(q.nstreams, fold_parts<D>()), kThreads, 0, st>>>(a, q, boundary);
+  const dim3 grid(q.nstreams, N4 / np);
+  if (np == 1) entry_fold_kernel<D, REV, TAN, 1><<<grid, kEpi, 0, st>>>(a, q, boundary);
+  else if (np == 2) entry_fold_kernel<D, REV, TAN, 2><<<grid, kEpi, 0, st>>>(a, q, boundary);
+  else if constexpr (NP_MAX >= 4) entry_fold_kernel<D, REV, TAN, 4><<<grid, kEpi, 0, st>>>(a, q, boundary);
   trace_after(tr, kTraceFold, st);
   count_launches(1);
   return cudaGetLastError();

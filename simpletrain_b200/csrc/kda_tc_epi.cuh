@@ -75,10 +75,13 @@ constexpr int kThreads = 64 + kEpi; // + TMA warp + MMA warp
 struct Epi {
   int et, lane, sp, cg, r0, cq;
   uint32_t lane_off;
-  __device__ Epi() {
-    et = threadIdx.x - 64;
-    lane = threadIdx.x & 31;
-    sp = (threadIdx.x >> 5) & 3;
+  __device__ Epi() : Epi((int)threadIdx.x) {}
+  // the geometry of CTA thread `tid` of the main kernels (warps 2 ..), for
+  // kernels that keep the carry layout without the producer warps
+  __device__ explicit Epi(int tid) {
+    et = tid - 64;
+    lane = tid & 31;
+    sp = (tid >> 5) & 3;
     cg = et >> 7;
     r0 = 16 * sp + (lane >> 2);
     cq = 2 * (lane & 3);
