@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kThreads + (agg_scales<PS, MODE>() ? 32 : 0), 
   // this CTA's range: the aggregate of the piece through which it publishes a carry
   // (reverse: a piece that ends at its stream's end starts with the ragged last chunk,
   // whose own decay factor multiplies a zero carry here and enters the consumer's A)
+  pdl_launch_dependents();  // entry_fold_kernel may start; it waits for this grid before reading
   const Span sp = span_of(qu, REV ? qu.nranges - 1 - (int)blockIdx.x : (int)blockIdx.x, REV);
   int stream, c_begin, c_end;
   if (!published_piece(qu, sp, REV, stream, c_begin, c_end)) return;
@@ -258,6 +259,7 @@ constexpr int kMaxFoldLinks = 1024;  // links whose chunk counts are staged in s
 
 template <int D, bool REV, bool TAN, int NP>
 __global__ void __launch_bounds__(kEpi) entry_fold_kernel(AggArgs a, Queue qu, const float *boundary) {
+  pdl_launch_dependents();  // the main kernel may start; its epilogue waits for this grid
   const int stream = (int)blockIdx.x;
   const long long first = (long long)stream * qu.nchunks;
   const int j_lo = range_of(qu, first), j_hi = range_of(qu, first + qu.nchunks - 1);
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(kEpi) entry_fold_kernel(AggArgs a, Queue qu, c
     for (int l = e.et; l < nlinks; l += kEpi) link_n[l] = link_chunks(l);
     __syncthreads();
   }
+  pdl_wait();  // the aggregates: agg_tc_kernel, launched just before this grid
 
   int n_prev = 0;
   bool tail_prev = false;
@@ -362,12 +365,14 @@ cudaError_t fold_launch(const AggArgs &a, const Queue &q, const float *boundary,
   while (np < NP_MAX && (long long)q.nstreams * (N4 / np) > 2LL * sms) np *= 2;
   const int tr = trace_before(st);
   const dim3 grid(q.nstreams, N4 / np);
-  if (np == 1) entry_fold_kernel<D, REV, TAN, 1><<<grid, kEpi, 0, st>>>(a, q, boundary);
-  else if (np == 2) entry_fold_kernel<D, REV, TAN, 2><<<grid, kEpi, 0, st>>>(a, q, boundary);
-  else if constexpr (NP_MAX >= 4) entry_fold_kernel<D, REV, TAN, 4><<<grid, kEpi, 0, st>>>(a, q, boundary);
+  cudaError_t e = cudaSuccess;
+  if (np == 1) e = launch_kernel(entry_fold_kernel<D, REV, TAN, 1>, grid, dim3(kEpi), 0, st, true, a, q, boundary);
+  else if (np == 2) e = launch_kernel(entry_fold_kernel<D, REV, TAN, 2>, grid, dim3(kEpi), 0, st, true, a, q, boundary);
+  else if constexpr (NP_MAX >= 4)
+    e = launch_kernel(entry_fold_kernel<D, REV, TAN, 4>, grid, dim3(kEpi), 0, st, true, a, q, boundary);
   trace_after(tr, kTraceFold, st);
   count_launches(1);
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int MODE>

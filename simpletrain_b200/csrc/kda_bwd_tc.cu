@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     __syncwarp();
   } else if (warp < kThreads / 32) {
     const Epi e;
+    pdl_wait();  // long streams: the entry carries come from entry_fold_kernel, launched just before
     Carry<D> Td;  // decay tangent (fp32 registers)
     Td.init_rows(e);
     float dl[Carry<D>::NR];  // this thread's share of dL/dlog decay for its rows
@@ -813,6 +814,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     __syncwarp();
   } else if (warp < kThreads / 32) {
     const Epi e;
+    pdl_wait();  // long streams: the entry carries come from entry_fold_kernel, launched just before
     Carry<D> dS;
     dS.init_rows(e);
     int gc = 0;
@@ -976,20 +978,22 @@ cudaError_t bwd_tc_launch(const BwdArgs &a, const Queue &q1, const Queue &q2, in
     if ((e = launch_agg_tc(PS ? 0 : 1, g, a.k, a.v, q1, dtype, a.s_in, st)) != cudaSuccess) return e;
   }
   int tr = trace_before(st);
-  k1<<<grid1, bwd_threads<PS>(), L1::SMEM, st>>>(mq, mk, mv, mg, mdy, mdq, mdg, mdo, a, q1);
+  e = launch_kernel(k1, dim3(grid1), dim3(bwd_threads<PS>()), L1::SMEM, st, q1.agg != nullptr, mq, mk, mv, mg, mdy,
+                    mdq, mdg, mdo, a, q1);
   trace_after(tr, kTraceBwdFwdDir, st);
   count_launches(1);
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (q2.agg) {  // long streams: dS aggregates from q and the dO the first pass wrote
     const AggArgs g{a.B, a.H, a.T, a.D, a.literal, a.per_step, a.decay, q2.agg, q2.agg_f4, a.status};
     if ((e = launch_agg_tc(2, g, a.q, a.dO, q2, dtype, a.ds_out, st)) != cudaSuccess) return e;
   }
   tr = trace_before(st);
-  k2<<<grid2, bwd_threads<PS>(), L2::SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, a, q2);
+  e = launch_kernel(k2, dim3(grid2), dim3(bwd_threads<PS>()), L2::SMEM, st, q2.agg != nullptr, mq, mk, mv, mdo, mdk,
+                    mdv, a, q2);
   trace_after(tr, kTraceBwdRevDir, st);
   count_launches(1);
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace

@@ -283,6 +283,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
   } else if (warp < kFwdThreads / 32) {
     // ----------------------------------------------------------- epilogue
     const Epi e;
+    pdl_wait();  // long streams: the entry carries come from entry_fold_kernel, launched just before
     Carry<D> S;
     S.init_rows(e);
     int gc = 0;
@@ -497,10 +498,11 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
     if (e != cudaSuccess) return e;
   }
   const int tr = trace_before(st);
-  kern<<<grid, fwd_threads<PS>(), L::SMEM, st>>>(mq, mk, mv, mg, my, a, q);
+  e = launch_kernel(kern, dim3(grid), dim3(fwd_threads<PS>()), L::SMEM, st, q.agg != nullptr, mq, mk, mv, mg, my, a,
+                    q);
   trace_after(tr, kTraceFwd, st);
   count_launches(1);
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <typename T, int D, bool LIT, bool PS, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>

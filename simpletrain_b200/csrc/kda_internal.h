@@ -65,6 +65,27 @@ __device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, in
 // Counts kernel launches for kda_launch_count().
 void count_launches(int n);
 
+// Launch `kern` on `st`.  With `early` the launch has a programmatic dependency
+// on the kernel before it on the stream: it may start while that kernel is still
+// running (once all of that kernel's CTAs have started or called
+// pdl_launch_dependents), and its threads call pdl_wait() before they read what
+// that kernel writes.
+template <typename... P, typename... A>
+cudaError_t launch_kernel(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool early,
+                          A &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = early ? attr : nullptr;
+  cfg.numAttrs = early ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<A &&>(args)...);
+}
+
 // kda_fwd_sm100's argument checks, all but the workspace's: KDA_OK or a kda_status.
 int fwd_check_args(const kda_fwd_params *p);
 
