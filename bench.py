@@ -8,11 +8,13 @@
 One step = one forward + backward pass of the KDA scan over one batch of the
 workload (default: the 1b-variant shape B=16, H=10, T=2048, D=128, chunk 64,
 bf16).  With N ranks the one global problem is sharded (``--scaling strong``,
-the default): the stream-major (stream, chunk) sequence is cut into N balanced
-ranges (``simpletrain_b200.sharding``); whole streams need no communication,
-and a stream that straddles two ranks (the 10b shape: 28 heads over 8 GPUs)
-is split in time with one small all_gather of carried states per direction.
-``value`` = the problem's tokens / the max-over-ranks device time per step.
+the default; ``simpletrain_b200.sharding``): each rank takes a run of whole
+streams (``--balance streams``, the default; no communication on the data
+path), or (``--balance chunks``) an exactly balanced range of the
+stream-major (stream, chunk) sequence, where a stream that straddles two
+ranks is split in time with one small all_gather of carried states per
+direction.  ``value`` = the problem's tokens / the max-over-ranks device time
+per step.
 ``--scaling weak`` gives every rank its own full batch instead.
 
 Each rank's step is captured once in a CUDA graph and replayed (the step's
@@ -219,7 +221,7 @@ def _run_ours(args, w, rank, world, local_rank, clk):
     fwd, bwd = cuda_scan_fns(w.chunk, mode)
     sworld, srank = (world, rank) if strong else (1, 0)
     sc = ShardedScan(B, H, T, D, w.chunk, sworld, srank, fwd=fwd, bwd=bwd,
-                     exchange=nccl_exchange() if sworld > 1 else None)
+                     exchange=nccl_exchange() if sworld > 1 else None, balance=args.balance)
     x = sc.load({"q": inp["q"], "k": inp["k"], "v": inp["v"], "g": inp["g"], "dy": inp["dy"],
                  "decay": decay, "s0": inp["s0"]})
     need_ds0 = inp["s0"] is not None
@@ -392,8 +394,10 @@ def _run_ours(args, w, rank, world, local_rank, clk):
 def config_dict(w, world, strong, sem_label, args):
     return dict(w.describe(), global_batch=w.B if strong else w.B * world, seq_len=w.T,
                 semantics=sem_label,
-                parallelism=(f"one problem sharded over {world} rank(s) by (stream, chunk) ranges; "
-                             "time-split streams exchange one carried state per direction"
+                parallelism=((f"one problem sharded over {world} rank(s) by whole (batch,head) streams; "
+                              "no data-path collective" if args.balance == "streams" else
+                              f"one problem sharded over {world} rank(s) by (stream, chunk) ranges; "
+                              "time-split streams exchange one carried state per direction")
                              if strong else f"(batch,head) weak scaling, {world} rank(s), no data-path collective"),
                 l2="inputs larger than L2 (no flush needed)")
 
@@ -747,6 +751,9 @@ def main():
     ap.add_argument("--workload", default="1b-fwdbwd", choices=sorted(WORKLOADS))
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: one problem sharded over the ranks (default); weak: a full batch per rank")
+    ap.add_argument("--balance", choices=["streams", "chunks"], default="streams",
+                    help="strong scaling: whole streams per rank (default), or exactly balanced chunk ranges "
+                         "with streams split in time between ranks")
     ap.add_argument("--shape", default=None,
                     help="B,H,T,D: run a custom shape (profiling / sweeps) instead of --workload")
     ap.add_argument("--fwd-only", action="store_true", help="with --shape: forward pass only")

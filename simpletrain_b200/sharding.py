@@ -1,10 +1,21 @@
 """The KDA scan of one fixed problem sharded over ranks, one process per GPU.
 
-Work unit: one chunk of one stream.  The ``B * H`` streams (stream index
-``s = b * H + h``) each have ``NC = ceil(T / C)`` chunks; the stream-major
-sequence of all ``B * H * NC`` chunks is cut into ``world`` contiguous,
-balanced ranges, one per rank (``shard_bounds``).  A rank's range splits at
-stream boundaries into pieces (``chunk_shard``):
+The ``B * H`` streams (stream index ``s = b * H + h``) are independent, so the
+default split (``balance="streams"``, ``stream_shard``) gives each rank a
+contiguous run of whole streams, ``floor`` or ``ceil`` of ``B * H / world``
+(``shard_bounds``), and the ranks never communicate.  When the stream count
+does not divide by the rank count the busiest rank holds one stream more than
+the least busy one; on the 10b shape (28 heads over 8 GPUs: four ranks with 4
+streams, four with 3) that costs less than splitting streams, because a
+rank's step time is dominated by per-launch costs at that size (one B200,
+fwd+bwd of 4 streams of 32768 tokens: 0.247 ms, of 3: 0.229 ms; with the
+time split below, 3.5 streams per rank over 8 GPUs: 0.587 ms per step).
+
+``balance="chunks"`` balances chunks exactly instead.  Work unit: one chunk
+of one stream; each stream has ``NC = ceil(T / C)`` chunks, and the
+stream-major sequence of all ``B * H * NC`` chunks is cut into ``world``
+contiguous, balanced ranges, one per rank (``shard_bounds``).  A rank's range
+splits at stream boundaries into pieces (``chunk_shard``):
 
 * whole streams ``[s0, s1)``;
 * at most one leading piece: the end (chunks ``[c0, NC)``) of a stream begun on
@@ -102,6 +113,14 @@ def chunk_shard(nstreams: int, nchunks: int, world: int, rank: int) -> List[Piec
             pieces.append(Piece(s, s + 1, c0, c1, nchunks))
             lo += c1 - c0
     return pieces
+
+
+def stream_shard(nstreams: int, nchunks: int, world: int, rank: int) -> List[Piece]:
+    """Rank's whole streams ``[s0, s1)`` (sizes differ by at most one), as one piece."""
+    if nstreams < world and nchunks > 0 and world > 1:
+        raise NotImplementedError(f"{nstreams} streams over {world} ranks: a rank would hold no stream")
+    s0, s1 = shard_bounds(nstreams, world, rank)
+    return [Piece(s0, s1, 0, nchunks, nchunks)] if s1 > s0 else []
 
 
 def splits_streams(nstreams: int, nchunks: int, world: int) -> bool:
@@ -219,6 +238,8 @@ class ShardedScan:
     ``[B, H, D, D]`` or None).  ``forward(x)`` and ``backward(x)`` run them with
     the exchanges described in the module docstring; each returns one dict per
     piece.  ``fwd``, ``bwd`` and ``exchange`` default to the CUDA ops and NCCL.
+    ``balance``: ``"streams"`` (whole streams per rank, no exchange) or
+    ``"chunks"`` (exactly balanced chunk ranges, streams split in time).
     The phases are also callable one by one (``forward_local``,
     ``forward_exit``, ``forward_rest``; ``backward_local``, ``backward_entry``,
     ``backward_rest``) for drivers that emulate several ranks in one process.
@@ -226,13 +247,17 @@ class ShardedScan:
 
     def __init__(self, B: int, H: int, T: int, D: int, chunk: int = 64, world: int = 1, rank: int = 0,
                  fwd: Optional[FwdFn] = None, bwd: Optional[BwdFn] = None,
-                 exchange: Optional[Callable[[Tensor], Tensor]] = None, mode: int = 0):
+                 exchange: Optional[Callable[[Tensor], Tensor]] = None, mode: int = 0,
+                 balance: str = "streams"):
+        if balance not in ("streams", "chunks"):
+            raise ValueError(f"balance must be 'streams' or 'chunks', not {balance!r}")
         self.B, self.H, self.T, self.D, self.chunk = B, H, T, D, chunk
-        self.world, self.rank = world, rank
+        self.world, self.rank, self.balance = world, rank, balance
         self.nchunks = (T + chunk - 1) // chunk
-        self.pieces = chunk_shard(B * H, self.nchunks, world, rank) if T > 0 else \
+        shard = chunk_shard if balance == "chunks" else stream_shard
+        self.pieces = shard(B * H, self.nchunks, world, rank) if T > 0 else \
             [Piece(*shard_bounds(B * H, world, rank), 0, 0, 0)]
-        self.split = T > 0 and splits_streams(B * H, self.nchunks, world)
+        self.split = T > 0 and balance == "chunks" and splits_streams(B * H, self.nchunks, world)
         if fwd is None or bwd is None:
             f, b = cuda_scan_fns(chunk, mode)
             fwd, bwd = fwd or f, bwd or b

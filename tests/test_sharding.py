@@ -15,7 +15,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from simpletrain_b200.sharding import (Piece, ShardedScan, chunk_shard, piece_param, piece_tensor,
-                                       shard_bounds, splits_streams)
+                                       shard_bounds, splits_streams, stream_shard)
 
 
 def test_shard_bounds_cover_and_balance():
@@ -53,6 +53,27 @@ def test_chunk_shard_tiles_the_chunk_sequence(nstreams, nchunks, world):
     assert max(sizes) - min(sizes) <= 1
     divisible = nstreams % world == 0
     assert splits_streams(nstreams, nchunks, world) == (not divisible and nchunks > 1)
+
+
+@pytest.mark.parametrize("nstreams,nchunks", [(160, 32), (28, 512), (5, 3), (3, 7)])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_stream_shard_gives_whole_streams(nstreams, nchunks, world):
+    if nstreams < world:
+        with pytest.raises(NotImplementedError):
+            stream_shard(nstreams, nchunks, world, 0)
+        return
+    per = []
+    for r in range(world):
+        ps = stream_shard(nstreams, nchunks, world, r)
+        assert len(ps) == 1 and ps[0].whole
+        per.append((ps[0].s0, ps[0].s1))
+    assert per[0][0] == 0 and per[-1][1] == nstreams
+    assert all(a[1] == b[0] for a, b in zip(per, per[1:]))
+    assert max(b - a for a, b in per) - min(b - a for a, b in per) <= 1
+    sc = ShardedScan(1, nstreams, nchunks * 64, 8, 64, world, 0, fwd=lambda *a: None, bwd=lambda *a: None)
+    assert not sc.split and sc.pieces == stream_shard(nstreams, nchunks, world, 0)
+    with pytest.raises(ValueError):
+        ShardedScan(1, nstreams, 64, 8, 64, world, 0, fwd=lambda *a: None, bwd=lambda *a: None, balance="x")
 
 
 def test_the_10b_shape_over_8_ranks_splits_four_heads_in_half():
@@ -146,7 +167,7 @@ def _problem(B, H, T, D):
     return x, dsT
 
 
-def _worker(rank, world, port, B, H, T, D, q):
+def _worker(rank, world, port, B, H, T, D, balance, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -154,7 +175,7 @@ def _worker(rank, world, port, B, H, T, D, q):
         torch.set_num_threads(1)
         x, dsT = _problem(B, H, T, D)
         fwd, bwd = _oracle_fns(64)
-        sc = ShardedScan(B, H, T, D, 64, world, rank, fwd=fwd, bwd=bwd, exchange=_exchange)
+        sc = ShardedScan(B, H, T, D, 64, world, rank, fwd=fwd, bwd=bwd, exchange=_exchange, balance=balance)
         loc = sc.load(x)
         outs = sc.forward(loc)
         dfin = [piece_param(dsT, p, B, H) if p.ends else None for p in sc.pieces]
@@ -177,17 +198,18 @@ def _worker(rank, world, port, B, H, T, D, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("B,H,T,world,split", [
-    (2, 3, 192, 2, False),     # 6 streams over 2 ranks: whole streams, no exchange
-    (1, 3, 200, 2, True),      # 3 streams of 4 chunks over 2 ranks: one stream split (ragged tail)
-    (1, 5, 130, 4, True),      # 15 chunks over 4 ranks: a rank with a leading and a trailing split
-    (2, 3, 256, 4, True),      # pieces that cross batch rows (copied, not viewed)
+@pytest.mark.parametrize("B,H,T,world,balance,split", [
+    (2, 3, 192, 2, "chunks", False),   # 6 streams over 2 ranks: whole streams, no exchange
+    (1, 3, 200, 2, "chunks", True),    # 3 streams of 4 chunks over 2 ranks: one stream split (ragged tail)
+    (1, 5, 130, 4, "chunks", True),    # 15 chunks over 4 ranks: a rank with a leading and a trailing split
+    (2, 3, 256, 4, "chunks", True),    # pieces that cross batch rows (copied, not viewed)
+    (2, 3, 200, 4, "streams", False),  # 6 whole streams over 4 ranks (2, 2, 1, 1), across batch rows
 ])
-def test_gloo_ranks_reassemble_the_unsharded_scan(B, H, T, world, split):
+def test_gloo_ranks_reassemble_the_unsharded_scan(B, H, T, world, balance, split):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, H, T, 8, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, H, T, 8, balance, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

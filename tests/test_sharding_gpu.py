@@ -29,9 +29,9 @@ def _needs_cuda():
     assert device_status() == 0, "a device-side bounded wait expired"
 
 
-def _emulate(B, H, T, D, world, inp, decay):
+def _emulate(B, H, T, D, world, inp, decay, balance="chunks"):
     fwd, bwd = cuda_scan_fns(64, 0)
-    scans = [ShardedScan(B, H, T, D, 64, world, r, fwd=fwd, bwd=bwd) for r in range(world)]
+    scans = [ShardedScan(B, H, T, D, 64, world, r, fwd=fwd, bwd=bwd, balance=balance) for r in range(world)]
     xs = [sc.load(dict(inp, decay=decay)) for sc in scans]
     with torch.inference_mode():
         outs = [sc.forward_local(x) for sc, x in zip(scans, xs)]
@@ -95,6 +95,22 @@ def test_emulated_ranks_match_one_gpu_and_the_oracle(B, H, T, world):
             assert e <= tol, (s, n, e)
         e = max_rel(got["ddecay"][b, h].cpu(), gr[4][0])
         assert e <= 2e-2, (s, "ddecay", e)
+
+
+@pytest.mark.parametrize("B,H,T,world", [
+    (1, 28, 2048, 8),     # the 10b head count over 8 ranks: 4, 4, 4, 4, 3, 3, 3, 3 whole streams
+    (2, 5, 700, 4),       # 3, 3, 2, 2 streams, runs across batch rows (copied), ragged last chunk
+])
+def test_whole_stream_shards_match_one_gpu(B, H, T, world):
+    D = 128
+    inp = make_inputs(custom(B, H, T, D, s0_std=0.02, decay_mean=4.0), seed=6, device=DEV)
+    scans, got = _emulate(B, H, T, D, world, inp, inp["decay"], balance="streams")
+    assert not scans[0].split and all(p.whole for sc in scans for p in sc.pieces)
+    ref = _unsharded(B, H, T, D, inp, inp["decay"])
+    for n in got:
+        tol = 1e-3 if n == "final_state" else 2e-2
+        e = max_rel(got[n].float().cpu(), ref[n].float().cpu())
+        assert e <= tol, (n, e)
 
 
 def test_forward_and_backward_replay_in_a_cuda_graph():
