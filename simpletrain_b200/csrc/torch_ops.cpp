@@ -20,6 +20,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <string>
 #include <tuple>
 #include <vector>
 
@@ -105,13 +106,18 @@ void decay_fields(const optional<Tensor> &decay, const float **p, int64_t *sb, i
 
 // state-update semantics of the ops: 0 = K^T V (chunk-constant decay), 1 = the
 // reference's literal K V^T, 2 = per-token decay
+// Error messages format integers with std::to_string, never by streaming them
+// into a std::ostream (which TORCH_CHECK does with its arguments): with this
+// toolchain and torch build, an integer streamed inside an extension module
+// crashed the process (SIGSEGV) instead of raising.
 uint32_t mode_flags(int64_t mode) {
-  TORCH_CHECK(mode >= 0 && mode <= 2, "mode must be 0 (corrected), 1 (literal) or 2 (per-step), got ", mode);
+  TORCH_CHECK(mode >= 0 && mode <= 2, "mode must be 0 (corrected), 1 (literal) or 2 (per-step), got ",
+              std::to_string(mode));
   return mode == 1 ? KDA_FLAG_LITERAL : (mode == 2 ? KDA_FLAG_PER_STEP : 0u);
 }
 
 void check(int rc, const char *what) {
-  TORCH_CHECK(rc == KDA_OK, what, " failed: ", kda_status_string(rc), " (status ", rc, ")");
+  TORCH_CHECK(rc == KDA_OK, what, " failed: ", kda_status_string(rc), " (status ", std::to_string(rc), ")");
 }
 
 void check_inputs(const Tensor &q, const Tensor &k, const Tensor &v, const optional<Tensor> &g) {

@@ -349,3 +349,33 @@ def test_kernel_trace_times_each_kernel_of_a_step():
     assert {n for n, _ in tr.launches} <= set(main) | {"agg_tc_kernel", "entry_fold_kernel"}
     per = tr.per_kernel()
     assert all(per[n][0] == 3 and 0.0 < per[n][1] < 100.0 for n in main)
+
+
+_BAD_CALLS = r"""
+import sys, torch
+import simpletrain_b200.ops  # noqa: F401
+q = torch.zeros(1, 2, 64, 128, device="cuda", dtype=torch.bfloat16)
+for args in ((q, q, q, None, None, 0.9, None, 64, 7, True),      # no such mode
+             (q, q, q, None, None, 0.01, None, 64, 2, True)):    # per-step decay below 0.125: the ABI refuses
+    try:
+        torch.ops.kda_b200.chunk_fwd(*args)
+        print("no error")
+    except RuntimeError as e:
+        print("raised", str(e).splitlines()[0])
+"""
+
+
+def test_op_argument_errors_raise_instead_of_crashing():
+    """Errors found in the C++ op (or reported by the C ABI) reach Python as
+    RuntimeError with the status text; run in a child process so a crash
+    cannot take the test session with it."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", _BAD_CALLS], cwd=root, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = out.stdout.strip().splitlines()
+    assert len(lines) == 2, out.stdout
+    assert lines[0].startswith("raised mode must be") and lines[0].endswith("got 7")
+    assert lines[1].startswith("raised kda_fwd_sm100 failed: unsupported configuration") and "(status 3)" in lines[1]
