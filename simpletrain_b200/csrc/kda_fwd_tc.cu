@@ -47,12 +47,23 @@ namespace kda {
 namespace {
 using namespace tc;
 
-#ifndef KDA_FWD_NS
-#define KDA_FWD_NS 2  // q/k/v stages
+// q/k/v stages and gate-in / y-out tiles per head dimension.  D=64: four stages
+// (three chunks of loads in flight; a chunk takes ~1.2 us there, less than the
+// loads' latency under load): 100m-shape forward 51.6 -> 49.0 us.  D=128: a third
+// stage fits only with two gate tiles, and that measured slower (1b shape 85 -> 95 us).
+#ifndef KDA_FWD_NS64
+#define KDA_FWD_NS64 4
 #endif
-#ifndef KDA_FWD_NY
-#define KDA_FWD_NY 4  // gate-in / y-out tiles
+#ifndef KDA_FWD_NS128
+#define KDA_FWD_NS128 2
 #endif
+#ifndef KDA_FWD_NY128
+#define KDA_FWD_NY128 4
+#endif
+template <int D>
+constexpr int fwd_ns() { return D == 64 ? KDA_FWD_NS64 : KDA_FWD_NS128; }
+template <int D>
+constexpr int fwd_ny() { return D == 64 ? 4 : KDA_FWD_NY128; }
 constexpr int kFwdThreads = kThreads;
 
 template <int D, int NS, int NY>
@@ -479,7 +490,7 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
   }
 }
 
-template <typename T, int D, bool LIT, bool PS, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
+template <typename T, int D, bool LIT, bool PS, int NS = fwd_ns<D>(), int NY = fwd_ny<D>()>
 cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream_t st) {
   constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv, mg, my;
@@ -505,7 +516,7 @@ cudaError_t fwd_tc_launch(const FwdArgs &a, const Queue &q, int grid, cudaStream
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-template <typename T, int D, bool LIT, bool PS, int NS = KDA_FWD_NS, int NY = KDA_FWD_NY>
+template <typename T, int D, bool LIT, bool PS, int NS = fwd_ns<D>(), int NY = fwd_ny<D>()>
 int fwd_ctas_per_sm() {
   auto kern = fwd_tc_kernel<T, D, LIT, PS, NS, NY>;
   int n = 0;
