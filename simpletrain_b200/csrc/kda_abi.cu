@@ -168,13 +168,13 @@ int ranges_override() {
 }
 
 // Ranges of one launch: one per resident CTA slot, at most one per chunk.  With
-// fewer streams than slots but at least half as many, one range per stream
+// fewer streams than slots but at least 3/5 as many, one range per stream
 // instead: cutting streams there puts ranges inside streams, whose carries then
 // need the range aggregates (a pass over k and v before the main kernel), and
-// that costs more than the idle slots.  Measured on 148 slots, forward /
-// backward: 128 streams of 32 chunks (D=128) 105 / 294 us cut, 68 / 226 us one
-// per stream; 96 streams 83 / 237 against 65 / 217; 64 streams of 64 chunks
-// 120 / 329 against 116 / 410, where cutting wins.
+// that costs more than the idle slots.  Measured on 148 slots, fwd+bwd per step,
+// D=128, streams of 32 chunks, one range per stream against cut: 120 streams
+// 0.293 / 0.350 ms, 104: 0.288 / 0.321, 96: 0.285 / 0.301, 88: 0.283 / 0.282,
+// 80: 0.286 / 0.267; D=64, 80 streams: 0.188 / 0.164.
 //
 // Cut ranges hold at least KDA_SM100_MIN_CHUNKS chunks (default 4): a range's
 // fixed cost (setting up its pipeline, the fold of its entry carry, its share
@@ -194,7 +194,7 @@ int n_ranges(int nstreams, int nchunks, int slots) {
   const long long n = (long long)nstreams * nchunks;
   long long want = slots;
   if (ranges_override() > 0) want = ranges_override();
-  else if (nstreams < slots && 2LL * nstreams >= slots) want = nstreams;
+  else if (nstreams < slots && 5LL * nstreams >= 3LL * slots) want = nstreams;
   else if (nstreams < slots) {
     const long long cap = (n + min_chunks_per_range() - 1) / min_chunks_per_range();
     if (cap < want) want = cap > nstreams ? cap : nstreams;
