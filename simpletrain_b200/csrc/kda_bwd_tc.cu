@@ -360,6 +360,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
         at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
       }
+      if (e.et == 0) KDA_TRACE_EVENT(16, gc);  // piece preamble done
       // per-step: carry factors a^kRef (operand of the first chunk), a^(64-kRef)
       // (tensor-memory carry -> state), the O row factors a^(row+1-kRef) for
       // rows r0 and r0 + 8, and the factor of this thread's dO row
@@ -605,6 +606,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         __stcg(slot + 2 * CF4 * kEpi + e.et, make_float4(dl[0], dl[Carry<D>::NR - 1], 0.f, 0.f));
         tc_fence_before();
         chain_publish(e, qu, u.pub_slot, 2);
+        if (e.et == 0) KDA_TRACE_EVENT(11, gc);  // exit carry published
       } else if (want_dd) {
         // <dS_T, T_T> row-wise, then the two column halves of every row meet in smem
         if (a.ds_out) {
