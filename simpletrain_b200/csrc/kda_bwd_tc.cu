@@ -340,6 +340,13 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       KDA_TAKE_UNIT(false)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
+      // chunk decays first: they do not depend on the boundary wait below
+      float af[Carry<D>::NR], at[Carry<D>::NR];
+      const int Ltail = a.T - (qu.nchunks - 1) * 64;
+      for (int r = 0; r < Carry<D>::NR; ++r) {
+        af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
+        at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
+      }
       // entry state and tangent: the initial ones, or the ones at the range boundary
       // (long streams: folded there before this kernel started; no wait)
       const bool fold = u.folds(qu);
@@ -352,13 +359,42 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       constexpr int CF4 = Carry<D>::FLOATS / 4;  // float4 per thread of one carry
       // the previous range's decay-gradient share is added at the end of the piece
       for (int r = 0; r < Carry<D>::NR; ++r) dl[r] = 0.f;
-      if (prev && !PS) Td.load_slot(e, prev + CF4 * kEpi);  // per-step mode carries no tangent
-      else Td.zero();
-      float af[Carry<D>::NR], at[Carry<D>::NR];
-      const int Ltail = a.T - (qu.nchunks - 1) * 64;
-      for (int r = 0; r < Carry<D>::NR; ++r) {
-        af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
-        at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
+      // D=128 (chunk-constant decay): the entry state goes to tensor memory here, its
+      // loads issued together with the tangent's, so the piece's first state step reads
+      // it from tensor memory like every later one instead of from global memory in
+      // four dependent column slices (tensor memory's state column block is free: the
+      // previous piece's last K^T V was read at its end, the next is issued after this
+      // piece's first state step)
+      bool entry_in_tmem = false;
+      if constexpr (D == 128 && !PS) {
+        if (prev || a.s_in) {
+          float4 v[CF4];
+          if (prev) {
+            for (int i4 = 0; i4 < CF4; ++i4) v[i4] = __ldcg(prev + i4 * kEpi + e.et);
+          } else {
+            const float4 *s4 = reinterpret_cast<const float4 *>(a.s_in + sbase + (size_t)Td.row[0] * D +
+                                                                 Carry<D>::W * e.cg);
+            for (int i4 = 0; i4 < CF4; ++i4) v[i4] = __ldg(s4 + i4);
+          }
+          if (prev) Td.load_slot(e, prev + CF4 * kEpi);
+          else Td.zero();
+          for (int half = 0; half < 2; ++half) {
+            uint32_t u32[32];
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 x = v[8 * half + q4];
+              u32[4 * q4] = __float_as_uint(x.x); u32[4 * q4 + 1] = __float_as_uint(x.y);
+              u32[4 * q4 + 2] = __float_as_uint(x.z); u32[4 * q4 + 3] = __float_as_uint(x.w);
+            }
+            tmem_st_32x32b_x32_nowait(tmem + e.lane_off + L::A_Z + Carry<D>::W * e.cg + 32 * half, u32);
+          }
+          tmem_wait_st();
+          entry_in_tmem = true;
+        } else {
+          Td.zero();
+        }
+      } else {
+        if (prev && !PS) Td.load_slot(e, prev + CF4 * kEpi);  // per-step mode carries no tangent
+        else Td.zero();
       }
       if (e.et == 0) KDA_TRACE_EVENT(16, gc);  // piece preamble done
       // per-step: carry factors a^kRef (operand of the first chunk), a^(64-kRef)
@@ -448,7 +484,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                 const uint32_t pb = sb + L::SB + (uint32_t)((col0 >> 6) * L::PANEL);
                 const uint32_t tz = tmem + e.lane_off + L::A_Z + col0, tw = tmem + e.lane_off + L::A_Y + col0;
                 uint32_t u32[SW], w32[SW];
-                if (c == u.c_begin) {
+                if (c == u.c_begin && !entry_in_tmem) {
                   if (prev) {
                     for (int q4 = 0; q4 < SW / 4; ++q4) {
                       const float4 v = __ldcg(prev + ((SW / 4) * sl + q4) * kEpi + e.et);
