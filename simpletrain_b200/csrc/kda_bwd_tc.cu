@@ -340,17 +340,20 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       KDA_TAKE_UNIT(false)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
-      // chunk decays first: they do not depend on the boundary wait below
+      // this thread's chunk decays: loaded before the boundary wait below (their round
+      // trip overlaps it), raised to the chunk lengths after it
       float af[Carry<D>::NR], at[Carry<D>::NR];
       const int Ltail = a.T - (qu.nchunks - 1) * 64;
-      for (int r = 0; r < Carry<D>::NR; ++r) {
-        af[r] = chunk_alpha(a.decay, b, h, Td.row[r], 64, 64);
-        at[r] = chunk_alpha(a.decay, b, h, Td.row[r], Ltail, 64);
-      }
+      for (int r = 0; r < Carry<D>::NR; ++r) af[r] = decay_value(a.decay, b, h, Td.row[r]);
       // entry state and tangent: the initial ones, or the ones at the range boundary
       // (long streams: folded there before this kernel started; no wait)
       const bool fold = u.folds(qu);
       if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      for (int r = 0; r < Carry<D>::NR; ++r) {
+        const float dv = af[r];
+        af[r] = chunk_alpha_of(a.decay, dv, 64, 64);
+        at[r] = chunk_alpha_of(a.decay, dv, Ltail, 64);
+      }
       if (e.et == 0 && i < 2) {
         KDA_TRACE_CTA(3 + 2 * i, kda_globaltimer());
         if (i == 0) KDA_TRACE_CTA(1, t);
@@ -860,18 +863,22 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
       KDA_TAKE_UNIT(true)
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
+      // this thread's chunk decays: loaded before the boundary wait below (their round
+      // trip overlaps it), raised to the chunk lengths after it
+      float af[Carry<D>::NR], at[Carry<D>::NR];
+      const int Ltail = a.T - (qu.nchunks - 1) * 64;
+      for (int r = 0; r < Carry<D>::NR; ++r) af[r] = decay_value(a.decay, b, h, dS.row[r]);
       // dS at the piece's end: the final-state gradient, or the one at the range boundary
       // (long streams: folded there before this kernel started; no wait)
       const bool fold = u.folds(qu);
       if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
+      for (int r = 0; r < Carry<D>::NR; ++r) {
+        const float dv = af[r];
+        af[r] = chunk_alpha_of(a.decay, dv, 64, 64);
+        at[r] = chunk_alpha_of(a.decay, dv, Ltail, 64);
+      }
       if (u.wait_slot < 0) dS.load_rm(e, a.ds_out ? a.ds_out + sbase : nullptr);
       else dS.load_slot(e, slot_ptr(qu, u.wait_slot));
-      float af[Carry<D>::NR], at[Carry<D>::NR];
-      const int Ltail = a.T - (qu.nchunks - 1) * 64;
-      for (int r = 0; r < Carry<D>::NR; ++r) {
-        af[r] = chunk_alpha(a.decay, b, h, dS.row[r], 64, 64);
-        at[r] = chunk_alpha(a.decay, b, h, dS.row[r], Ltail, 64);
-      }
       // per-step: W factor a^kRef, operand factor a^(L-kRef) for the chunk that
       // reads it (full, or the stream's tail chunk first), dk row factors a^(kRef-1-row)
       float am = 1.f, ad_f = 1.f, ad_0 = 1.f, rk[2] = {1.f, 1.f};

@@ -306,24 +306,28 @@ __global__ void __launch_bounds__(fwd_threads<PS>(), 1)
       const Piece u = piece_of(qu, span_of(qu, t, false), p, false);
       const int b = u.stream / a.H, h = u.stream - b * a.H;
       const size_t sbase = (size_t)u.stream * D * D;
+      // this thread's chunk decays: loaded before the boundary wait below (their round
+      // trip overlaps it), raised to the chunk lengths after it
+      float af[Carry<D>::NR], at[Carry<D>::NR];
+      const int Ltail = a.T - (qu.nchunks - 1) * 64;
+      for (int r = 0; r < Carry<D>::NR; ++r) af[r] = decay_value(a.decay, b, h, S.row[r]);
       // piece-start state: the initial state, or the one at the range boundary
       // (long streams: folded there before this kernel started; no wait)
       const bool fold = u.folds(qu);
       if (e.et == 0) KDA_TRACE_EVENT(15, gc);
       if (!fold && !chain_wait(e, qu, u.wait_slot, a.status, abort_flag)) break;
       if (e.et == 0) KDA_TRACE_EVENT(16, gc);
+      for (int r = 0; r < Carry<D>::NR; ++r) {
+        const float dv = af[r];
+        af[r] = chunk_alpha_of(a.decay, dv, 64, 64);
+        at[r] = chunk_alpha_of(a.decay, dv, Ltail, 64);
+      }
       if (e.et == 0 && i == 0) {
         KDA_TRACE_CTA(4, kda_globaltimer());
         KDA_TRACE_CTA(6, t);
       }
       if (u.wait_slot < 0) S.load_rm(e, a.s_in ? a.s_in + sbase : nullptr);
       else S.load_slot(e, slot_ptr(qu, u.wait_slot));
-      float af[Carry<D>::NR], at[Carry<D>::NR];
-      const int Ltail = a.T - (qu.nchunks - 1) * 64;
-      for (int r = 0; r < Carry<D>::NR; ++r) {
-        af[r] = chunk_alpha(a.decay, b, h, S.row[r], 64, 64);
-        at[r] = chunk_alpha(a.decay, b, h, S.row[r], Ltail, 64);
-      }
       // per-step: operand a^kRef S, U factor a^(L-kRef) (full / tail chunk),
       // y row factors a^(row+1-kRef) for rows r0 and r0 + 8
       float am = 1.f, au_f = 1.f, au_t = 1.f, rq[2] = {1.f, 1.f};

@@ -62,6 +62,13 @@ __device__ __forceinline__ float decay_value(const DecaySrc &s, int b, int h, in
   return s.ptr[b * s.sb + h * s.sh + d * s.sd];
 }
 
+// chunk_alpha from a value decay_value() loaded earlier (the load's latency can then
+// overlap other waits); the same result as chunk_alpha.
+__device__ __forceinline__ float chunk_alpha_of(const DecaySrc &s, float dv, int L, int C) {
+  if (s.ptr == nullptr) return (L == C) ? s.alpha_full : s.alpha_tail;
+  return powf(dv, (float)L);
+}
+
 // Counts kernel launches for kda_launch_count().
 void count_launches(int n);
 

@@ -565,11 +565,13 @@ __device__ __forceinline__ bool shares_wait(const Epi &e, const Queue &qu, int l
 }
 
 // Epilogue: after every thread stored its part of the slot, publish it.  The
-// barrier orders the other threads' stores before thread 0's fence, which is
-// cumulative, so one fence suffices.
+// barrier orders the other threads' stores before the publishing thread's fence,
+// which is cumulative, so one fence suffices.  The last epilogue thread publishes:
+// thread 0 waits for the next piece's boundary flag (chain_wait), so the fence's
+// round trip and that flag's overlap instead of adding up.
 __device__ __forceinline__ void chain_publish(const Epi &e, const Queue &qu, int slot, int level = 1) {
   named_bar_sync(1, kEpi);
-  if (e.et == 0) {
+  if (e.et == kEpi - 1) {
     __threadfence();
     atomicExch(qu.flags + slot, level);
   }
