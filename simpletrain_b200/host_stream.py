@@ -269,27 +269,33 @@ class ShardedHostScan:
     device on a copy-in stream, runs the forward (and the backward when the
     pieces carry ``dy``) with the scan's exchanges on a compute stream, and
     copies every result back to pinned host buffers on a copy-out stream.  It
-    returns at once with a ``Pending``; device inputs and host results come in
-    two sets used in turn, so step i+1's copies in run while step i computes
-    and step i-1's results come back, and the two PCIe directions overlap.
-    Results: per piece a dict with ``y``, ``final_state`` and, with ``dy``,
-    ``dq``, ``dk``, ``dv``, ``dg``, ``ddecay`` (a tensor decay), ``ds0`` (a
-    piece that holds the stream's initial state).  A call's results stay
-    valid until the second submission after it, which first waits for it.
-    All ranks must submit the same number of steps (the exchanges are
-    collectives).
+    returns with a ``Pending``; device inputs and host results come in
+    ``sets`` sets (default 2) used in turn, so step i+1's copies in run while
+    step i computes and step i-1's results come back, and the two PCIe
+    directions overlap.  A submission queues its copies in and its scan at
+    once and waits on the host only before queueing its copies out, for the
+    call that last used its set.  Results: per piece a dict with ``y``,
+    ``final_state`` and, with ``dy``, ``dq``, ``dk``, ``dv``, ``dg``,
+    ``ddecay`` (a tensor decay), ``ds0`` (a piece that holds the stream's
+    initial state).  A call's results stay valid until the ``sets``-th
+    submission after it, which first waits for it: with three sets a caller
+    can read step i-2's results after submitting step i and keep both copy
+    directions busy.  All ranks must submit the same number of steps (the
+    exchanges are collectives).
     """
 
     def __init__(self, scan, device: Optional[Union[int, str, torch.device]] = None,
-                 need_ddecay: bool = True, need_ds0: bool = True):
+                 need_ddecay: bool = True, need_ds0: bool = True, sets: int = 2):
+        if sets < 2:
+            raise ValueError("ShardedHostScan needs at least two buffer sets")
         self.scan = scan
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.need = (need_ddecay, need_ds0)
         self._streams = [torch.cuda.Stream(device=self.device) for _ in range(3)]
-        self._dev = [None, None]       # device inputs per buffer set
-        self._host = [None, None]      # pinned host results per buffer set
-        self._busy = [None, None]      # per set: the event after which its device inputs are free
-        self._pending = [None, None]
+        self._dev = [None] * sets      # device inputs per buffer set
+        self._host = [None] * sets     # pinned host results per buffer set
+        self._busy = [None] * sets     # per set: the event after which its device inputs are free
+        self._pending = [None] * sets
         self._turn = 0
 
     @staticmethod
@@ -304,12 +310,14 @@ class ShardedHostScan:
         s_in, s_run, s_out = self._streams
         caller = torch.cuda.current_stream(self.device)
         turn = self._turn
-        self._turn ^= 1
-        if self._pending[turn] is not None:
-            self._pending[turn].wait()
+        self._turn = (turn + 1) % len(self._dev)
         if self._dev[turn] is None:
             self._dev[turn] = [self._to_device_like(p, self.device) for p in pieces]
         dev = self._dev[turn]
+        # Copies in and the scan are queued before the host waits for anything: they depend
+        # only on device work (the scan that last read these device buffers), so the copy-in
+        # stream never runs dry while the host waits; only the copies out, which overwrite
+        # the result buffers of the call two submissions back, are queued after that wait.
         with torch.cuda.stream(s_in):
             s_in.wait_stream(caller)
             if self._busy[turn] is not None:
@@ -331,6 +339,8 @@ class ShardedHostScan:
             done = torch.cuda.Event()
             done.record(s_run)
         self._busy[turn] = done
+        if self._pending[turn] is not None:
+            self._pending[turn].wait()
         if self._host[turn] is None:
             self._host[turn] = [{n: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for n, t in o.items()}
                                 for o in outs]

@@ -130,3 +130,48 @@ def test_host_scan_submitted_calls_overlap_and_keep_their_results():
     got.append({n: t.clone() for n, t in pend.wait().items()})
     for (q, k, v, g, dy, _), res in zip(batches, got):
         _check(res, _device_reference(q, k, v, g, decay, dy, None))
+
+
+def _pinned_copy(t):
+    if not torch.is_tensor(t):
+        return t
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t)
+    return h
+
+
+@pytest.mark.parametrize("sets,lag", [(2, 1), (3, 2)])
+def test_sharded_host_scan_pipelined_steps(sets, lag):
+    """ShardedHostScan (one rank): consecutive steps with different inputs, each
+    step submitted before step i-lag's results are read -- the pattern bench.py's
+    end-to-end number uses with three buffer sets -- give every step the results
+    of the same scan run directly on the device."""
+    from simpletrain_b200.host_stream import ShardedHostScan
+    from simpletrain_b200.sharding import ShardedScan
+
+    B, H, T, D = 2, 4, 700, 128
+    decay = torch.sigmoid(torch.randn(H, D, generator=torch.Generator().manual_seed(3)) + 3.0)
+    steps = 5
+    data = [_inputs(B, H, T, D, seed=40 + i) for i in range(steps)]
+    sc = ShardedScan(B, H, T, D, 64, 1, 0)
+    runner = ShardedHostScan(sc, DEV, True, False, sets=sets)
+    hosts = []
+    for q, k, v, g, dy, _ in data:
+        pieces = sc.load({"q": q, "k": k, "v": v, "g": g, "dy": dy, "decay": decay, "s0": None})
+        hosts.append([{n: _pinned_copy(t) for n, t in p.items()} for p in pieces])
+    pend, got = [], []
+    for i in range(steps + lag):
+        if i < steps:
+            pend.append(runner.submit(hosts[i]))
+        if i >= lag:
+            res = pend[i - lag].wait()
+            got.append({n: t.clone() for n, t in res[0].items()})
+    assert len(got) == steps
+    for (q, k, v, g, dy, _), out in zip(data, got):
+        ref = _device_reference(q, k, v, g, decay, dy, None)
+        for n in ("y", "final_state", "dq", "dk", "dv", "dg"):
+            tol = 1e-4 if n == "final_state" else 8e-3
+            e = max_rel(out[n].float(), ref[n].float().cpu())
+            assert e <= tol, (n, e)
+        e = max_rel(out["ddecay"].float().sum(0).reshape(H, D), ref["ddecay"].float().cpu().reshape(H, D))
+        assert e <= 1e-4, ("ddecay", e)
