@@ -335,6 +335,12 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
     Td.init_rows(e);
     float dl[Carry<D>::NR];  // this thread's share of dL/dlog decay for its rows
     float *red = reinterpret_cast<float *>(smem + L::RED);
+#ifdef KDA_TRACE
+    // trace build: per-CTA totals of the epilogue's waits and steps (cycles)
+    long long tw_full = 0, tw_qk = 0, tw_dp = 0, tw_s = 0, tw_o = 0, tw_dq = 0;
+    long long ts_do = 0, ts_mask = 0, ts_rd = 0, ts_state = 0, ts_dg = 0, ts_dq = 0;
+    long long ts_sl = 0, ts_wst = 0, ts_sync = 0;
+#endif
     int gc = 0;
     for (int i = 0;; ++i) {
       KDA_TAKE_UNIT(false)
@@ -416,7 +422,8 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         const int s = gc % NS, use = gc / NS, ph = gc & 1;
         const uint32_t st = sb + s * L::STAGE;
         const int t0 = 64 * c, Lc = min(64, a.T - t0);
-        if (!(ok = mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag))) break;
+        if (!(ok = KDA_TIMED(tw_full, mbar_wait(bar(FULL + s), use & 1, a.status, abort_flag)))) break;
+        KDA_CLK(kc0);
         if (e.et == 0) KDA_TRACE_EVENT(0, gc);
         // (0) dO (the DO tile's last readers were the previous chunk's MMAs)
         if (e.et == 0) KDA_TRACE_EVENT(27, gc);
@@ -433,13 +440,15 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           tma_store_commit();
           KDA_TRACE_EVENT(1, gc);
         }
+        KDA_ADD(ts_do, kc0);
+        KDA_CLK(kc1);
         // (a) P, (b) dP
-        if (!(ok = mbar_wait(bar(QK_FULL), ph, a.status, abort_flag))) break;
+        if (!(ok = KDA_TIMED(tw_qk, mbar_wait(bar(QK_FULL), ph, a.status, abort_flag)))) break;
         if (e.et == 0) KDA_TRACE_EVENT(5, gc);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_QK, sb + L::P);
         if (e.et == 0) KDA_TRACE_EVENT(31, gc);
-        if (!(ok = mbar_wait(bar(DP_FULL), ph, a.status, abort_flag))) break;
+        if (!(ok = KDA_TIMED(tw_dp, mbar_wait(bar(DP_FULL), ph, a.status, abort_flag)))) break;
         if (e.et == 0) KDA_TRACE_EVENT(6, gc);
         tc_fence_after();
         masked_tile<BF>(e, tmem + e.lane_off + L::A_DP, sb + L::DP);
@@ -447,7 +456,9 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         if (e.et == 0) {
           // this chunk's dO store has read the DO tile (rewritten next chunk), and the last
           // chunk's dg / dq stores have read its stage: hand that stage back
+          KDA_CLK(kr);
           tma_store_wait_read<0>();
+          KDA_ADD(ts_rd, kr);
           if (gc > 0) mbar_arrive(bar(EMPTY + (gc - 1) % NS));
         }
         named_bar_sync(1, kEpi);
@@ -456,10 +467,12 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           mbar_arrive(bar(DPM_FULL));
           KDA_TRACE_EVENT(7, gc);
         }
+        KDA_ADD(ts_mask, kc1);
+        KDA_CLK(kc2);
         // (s) state step: S_{c-1} -> operand, decay^L S_{c-1} -> tensor memory,
         //     decay term <T_{c-1}, W_c>, tangent update; column slices of 32
-        if (c > u.c_begin && !(ok = mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag))) break;
-        if (!(ok = mbar_wait(bar(W_FULL), ph, a.status, abort_flag))) break;
+        if (c > u.c_begin && !(ok = KDA_TIMED(tw_s, mbar_wait(bar(KV_FULL), (gc - 1) & 1, a.status, abort_flag)))) break;
+        if (!(ok = KDA_TIMED(tw_s, mbar_wait(bar(W_FULL), ph, a.status, abort_flag)))) break;
         if (e.et == 0) KDA_TRACE_EVENT(2, gc);
         tc_fence_after();
         {
@@ -542,9 +555,13 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
                 else tmem_st_32x32b_x32_nowait(tz, u32);
               }
             };
+            KDA_CLK(ks0);
             if (want_dd) slices(std::integral_constant<int, 16>{});
             else slices(std::integral_constant<int, 32>{});
+            KDA_ADD(ts_sl, ks0);
+            KDA_CLK(ks1);
             tmem_wait_st();
+            KDA_ADD(ts_wst, ks1);
           } else {
             Carry<D> Sp;
             Sp.row[0] = Td.row[0];
@@ -574,6 +591,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           }
         }
         if (e.et == 0) KDA_TRACE_EVENT(3, gc);
+        KDA_CLK(ks2);
         fence_async_smem();
         tc_fence_before();
         named_bar_sync(1, kEpi);
@@ -581,8 +599,11 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           mbar_arrive(bar(S_READY));
           KDA_TRACE_EVENT(4, gc);
         }
+        KDA_ADD(ts_sync, ks2);
+        KDA_ADD(ts_state, kc2);
+        KDA_CLK(kc3);
         // (c) dg = dy * O over the dy tile, then a TMA store
-        if (!(ok = mbar_wait(bar(O_FULL), ph, a.status, abort_flag))) break;
+        if (!(ok = KDA_TIMED(tw_o, mbar_wait(bar(O_FULL), ph, a.status, abort_flag)))) break;
         if (e.et == 0) KDA_TRACE_EVENT(8, gc);
         tc_fence_after();
         if (gate) {
@@ -595,8 +616,10 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           }
         }
         if (e.et == 0) KDA_TRACE_EVENT(9, gc);
+        KDA_ADD(ts_dg, kc3);
+        KDA_CLK(kc4);
         // (d) dq over the stage's gate tile (read only by the dO step), then a TMA store
-        if (!(ok = mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag))) break;
+        if (!(ok = KDA_TIMED(tw_dq, mbar_wait(bar(DQ_FULL), ph, a.status, abort_flag)))) break;
         tc_fence_after();
         frag_to_tile<D, BF>(e, tmem + e.lane_off + A_DQ, st + L::ST_G, 0, false);
         tc_fence_before();
@@ -609,6 +632,7 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
           KDA_TRACE_EVENT(10, gc);
         }
         if (e.et == 0) KDA_TRACE_EVENT(12, gc);
+        KDA_ADD(ts_dq, kc4);
       }
       if (!ok) break;
       if (e.et == 0 && i < 2) KDA_TRACE_CTA(4 + 2 * i, kda_globaltimer());
@@ -667,6 +691,16 @@ __global__ void __launch_bounds__(bwd_threads<PS>(), 1)
         }
         tc_fence_before();
       }
+    }
+    if (e.et == 0) {  // trace build: per-CTA totals (cycles) of waits and steps
+      KDA_TRACE_CTA(8, tw_s);
+      KDA_TRACE_CTA(9, ts_do);
+      KDA_TRACE_CTA(10, ts_mask);
+      KDA_TRACE_CTA(11, ts_sl);
+      KDA_TRACE_CTA(12, ts_state);
+      KDA_TRACE_CTA(13, ts_wst);
+      KDA_TRACE_CTA(14, ts_sync);
+      KDA_TRACE_CTA(15, gc);
     }
   } else if constexpr (PS) {
     scaler_role<D, BF, NS>(qu, false, a.H, a.decay, sb, L::STAGE, L::ST_K, warp - kThreads / 32, ring, abort_flag,

@@ -28,19 +28,29 @@
 // Development tracing: built only with -DKDA_TRACE (python -m simpletrain_b200.build
 // --trace writes a separate library); records clock64() of pipeline events of
 // CTA 0 into a per-kernel-file device array [chunk][32 slots], and the global
-// timer (ns) of per-CTA milestones into [CTA][8 slots] (slot 7: SM id).
+// timer (ns) of per-CTA milestones into [CTA][16 slots] (slot 7: SM id).
 #ifdef KDA_TRACE
 #define KDA_TRACE_DEFINE                                      \
   static __device__ unsigned long long g_kda_trace[128 * 32]; \
-  static __device__ unsigned long long g_kda_trace_cta[1024 * 8];
+  static __device__ unsigned long long g_kda_trace_cta[1024 * 16];
 #define KDA_TRACE_EVENT(slot, chunk)                                                    \
   do {                                                                                  \
     if (blockIdx.x == 0 && (chunk) < 128) g_kda_trace[(chunk) * 32 + (slot)] = clock64(); \
   } while (0)
-#define KDA_TRACE_CTA(slot, value)                                              \
-  do {                                                                          \
-    if (blockIdx.x < 1024) g_kda_trace_cta[blockIdx.x * 8 + (slot)] = (value); \
+#define KDA_TRACE_CTA(slot, value)                                               \
+  do {                                                                           \
+    if (blockIdx.x < 1024) g_kda_trace_cta[blockIdx.x * 16 + (slot)] = (value); \
   } while (0)
+// cycles spent in `expr` (a wait) added to `acc`
+#define KDA_TIMED(acc, expr)                  \
+  ([&]() {                                    \
+    const long long kda_t0_ = clock64();      \
+    const auto kda_r_ = (expr);               \
+    (acc) += clock64() - kda_t0_;             \
+    return kda_r_;                            \
+  }())
+#define KDA_CLK(v) const long long v = clock64()
+#define KDA_ADD(acc, from) (acc) += clock64() - (from)
 __device__ __forceinline__ unsigned long long kda_globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -59,6 +69,9 @@ __device__ __forceinline__ unsigned kda_smid() {
 #define KDA_TRACE_CTA(slot, value) \
   do {                             \
   } while (0)
+#define KDA_TIMED(acc, expr) (expr)
+#define KDA_CLK(v)
+#define KDA_ADD(acc, from)
 #endif
 
 namespace kda {
